@@ -1,0 +1,408 @@
+"""Benchmark of the paged GQA decode-attention hot path on B200.
+
+Default workload (BASELINE config 2's target point): B = 256 sequences x
+kv_len 4096, 14 q / 2 kv heads, head_dim 64, 16-token pages scattered by a
+random permutation over the pool, fp16 N(0, 1) data. One step = one call of
+the decode-attention op over the batch (split-KV load, plus merge when the
+split count is above 1).
+
+Metric: algorithmic HBM GB/s = (K/V rows read + q read + o written +
+block-table entries read) / time, summed over ranks (each rank owns its own
+batch and KV pool: sequences are sharded, no collective on the data path).
+
+Legs:
+  value     device time (CUDA events on the launching stream) of K steps
+            with all inputs resident; inputs (537 MB of K/V) exceed L2.
+  e2e       the same metric through the C ABI with HOST buffers: every step
+            copies q, the K/V pools, lens, slot ids and the block table from
+            pinned host memory and reads the output back.
+  roofline  dominant kernel's achieved algorithmic GB/s / measured HBM peak.
+  cpu_baseline  the CPU oracle (torch fp32 gather + softmax) on the host's
+            cores over a bounded sample of the same workload.
+
+``--impl reference`` times the reference attention math on the host CPU
+(the oracle port: the reference engine ships no CPU kernel of its own and
+its Triton kernels need a GPU) on the same config, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "paged decode-attn HBM GB/s (% peak)"
+UNIT = "GB/s"
+H_Q, H_KV, D, PAGE = 14, 2, 64, 16
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--kv-len", type=int, default=4096)
+    ap.add_argument("--splits", type=int, default=0, help="KV splits (0 = library default)")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="bound on the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args(argv)
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (one process per GPU, NCCL only for results)
+# ---------------------------------------------------------------------------
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def dist_barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def dist_max(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def dist_sum(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def dist_done(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# measurement helpers
+# ---------------------------------------------------------------------------
+
+def measured_peak_gbs():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic_per_launch(batch: int, kv_len: int):
+    """dram read+write bytes per launch of the decode kernel from the committed
+    ncu summary of this workload, if there is one."""
+    p = REPO / "profiles" / f"decode_split_kernel_b{batch}_l{kv_len}.md"
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", p.read_text())
+    return int(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.lines = []
+        try:
+            bus = torch.cuda.get_device_properties(device_index).pci_bus_id
+        except Exception:
+            bus = None
+        self.bus = bus
+
+    def __enter__(self):
+        if self.bus is None:
+            return self
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.bus)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() in ("active", "1"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def decode_bytes(batch: int, kv_len: int) -> int:
+    kv = batch * kv_len * H_KV * D * 2 * 2
+    qo = batch * H_Q * D * 2 * 2
+    bt = batch * math.ceil(kv_len / PAGE) * 8
+    return kv + qo + bt
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle port)
+# ---------------------------------------------------------------------------
+
+def cpu_oracle_rate(kv_len: int, seconds: float, max_seqs: int = 64):
+    """Times the fp32 CPU oracle on sequences of ``kv_len`` until ``seconds``
+    elapse; returns (GB/s, threads, sample description)."""
+    import oracle
+    from custom_inference_engine_b200 import workloads as W
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    per = 4
+    c = W.make_decode_case([kv_len] * per, seed=3)
+    oracle.decode_attention_fp32(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table)  # warm
+    t0 = time.perf_counter()
+    done = 0
+    while done < max_seqs:
+        oracle.decode_attention_fp32(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table)
+        done += per
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    nbytes = decode_bytes(done, kv_len)
+    return nbytes / dt / 1e9, threads, f"{done} sequences x kv_len {kv_len} ({dt:.1f} s)"
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference attention math on the host CPU."""
+    if rank != 0:
+        return None
+    per_step = max(1, min(args.batch, 8))
+    import oracle
+    from custom_inference_engine_b200 import workloads as W
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    c = W.make_decode_case([args.kv_len] * per_step, seed=3)
+    warm = max(3, min(args.warmup, 5))
+    for _ in range(warm):
+        oracle.decode_attention_fp32(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table)
+    t0 = time.perf_counter()
+    steps = 0
+    while steps < args.steps:
+        oracle.decode_attention_fp32(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table)
+        steps += 1
+        if time.perf_counter() - t0 > args.cpu_seconds * 4:
+            break
+    dt = time.perf_counter() - t0
+    gbs = decode_bytes(per_step, args.kv_len) * steps / dt / 1e9
+    sample = (f"{per_step} of {args.batch} sequences x kv_len {args.kv_len} per step, "
+              f"{steps} steps")
+    return {
+        "metric": METRIC, "value": gbs, "unit": UNIT, "impl": "reference",
+        "n_gpus": world, "steps": steps, "warmup": warm,
+        "ms_per_step": dt / steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 (fp16 inputs)", "data": "synthetic",
+        "config": workload_config(args, world),
+        "cpu_baseline": {"value": gbs, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": gbs, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def workload_config(args, world):
+    return {
+        "workload": (f"paged GQA decode attention, B={args.batch} x kv_len {args.kv_len}, "
+                     f"14q/2kv heads, D=64, page 16, random page permutation"),
+        "batch_per_gpu": args.batch, "kv_len": args.kv_len, "heads_q": H_Q, "heads_kv": H_KV,
+        "head_dim": D, "page_size": PAGE, "parallelism": f"sequence-sharded x{world}",
+        "l2": "inputs larger than L2 (K/V pools %.0f MB per GPU)" % (
+            args.batch * args.kv_len * 512 / 1e6),
+    }
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank, world, local):
+    from custom_inference_engine_b200 import cabi, native
+    from custom_inference_engine_b200 import workloads as W
+    from custom_inference_engine_b200.attn import core
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B, L = args.batch, args.kv_len
+    c = W.make_decode_case([L] * B, seed=100 + rank, device=dev, generate_on_device=True)
+    S = args.splits if args.splits > 0 else cabi.decode_default_splits(B, dev.index)
+    launches_per_step = 1 if S == 1 else 2
+    native.device_errors(dev.index, clear=True)
+
+    def step():
+        return core.decode_gqa_attention(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table,
+                                         num_programs=S)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clocks:
+        events[0].record(stream)
+        for i in range(args.steps):
+            step()
+            events[i + 1].record(stream)
+        torch.cuda.synchronize()
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    per_step_ms = [events[i].elapsed_time(events[i + 1]) for i in range(args.steps)]
+    local_ms = events[0].elapsed_time(events[-1])
+    total_ms = dist_max(local_ms, world, dev)
+    nbytes = decode_bytes(B, L)
+    value = nbytes * world * args.steps / (total_ms / 1e3) / 1e9
+    kernel_ms = statistics.mean(per_step_ms)
+    achieved = nbytes / (kernel_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    errs = native.device_errors(dev.index, clear=True)
+
+    # ---- e2e: C ABI with host buffers ---------------------------------------
+    host = {n: getattr(c, n).cpu().pin_memory()
+            for n in ("q", "k", "v", "lens", "slot_ids", "block_table")}
+    dbuf = {n: torch.empty_like(getattr(c, n)) for n in host}
+    out_dev = torch.empty_like(c.q)
+    out_host = torch.empty(c.q.shape, dtype=c.q.dtype).pin_memory()
+    ws_bytes = cabi.decode_workspace_bytes(B, H_Q, D, S)
+    ws = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device=dev)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        for n in host:
+            dbuf[n].copy_(host[n], non_blocking=True)
+        cabi.decode_attention(dbuf["q"], dbuf["k"], dbuf["v"], dbuf["lens"], dbuf["slot_ids"],
+                              dbuf["block_table"], out=out_dev, num_splits=S,
+                              workspace=ws if ws_bytes else None)
+        out_host.copy_(out_dev, non_blocking=True)
+
+    e2e_steps = max(1, args.e2e_steps)
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = dist_max(e0.elapsed_time(e1), world, dev)
+    e2e_value = nbytes * world * e2e_steps / (e2e_ms / 1e3) / 1e9
+    ok = torch.equal(out_host, step().cpu())
+
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16 in / fp32 accumulate", "data": "synthetic",
+            "config": dict(workload_config(args, world), num_splits=S),
+            "pct_of_peak": 100.0 * achieved / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                         "traffic": ncu_traffic_per_launch(B, L),
+                         "algorithmic_bytes_per_launch": nbytes,
+                         "kernel": "decode_split_kernel<2>" + (" + decode_merge_kernel"
+                                                               if S > 1 else "")},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "path": "cie_decode_attention via ctypes, pinned host buffers",
+                    "output_matches_device_leg": bool(ok)},
+            "gpu_launches": args.steps * launches_per_step,
+            "clocks": clocks.summary(),
+            "device_error_bits": errs,
+        }
+        if not args.no_cpu_baseline and world == 1:
+            gbs, cores, sample = cpu_oracle_rate(L, args.cpu_seconds)
+            result["cpu_baseline"] = {"value": gbs, "unit": UNIT, "cores": cores, "kind": "port",
+                                      "sample": sample}
+    return result
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    rank, world, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            res = run_reference(args, rank, world)
+        else:
+            res = run_ours(args, rank, world, local)
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        dist_done(world)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,89 @@
+"""Builds the two native libraries of the package, in-tree, for sm_100a.
+
+* ``libcie_attention.so`` -- the CUDA kernels and their C ABI
+  (``include/cie_attention.h``), compiled by nvcc from ``csrc/cie_unity.cu``;
+  the CUDA runtime is linked statically and its symbols are not exported.
+* ``_cie_torch_ops.so`` -- the ``inference::*`` torch ops
+  (``csrc/torch_ops.cpp``) linked against the library above
+  (rpath ``$ORIGIN``), built with ``torch.utils.cpp_extension``.
+
+Both land next to this file so they travel with the source tree.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+REPO = PKG.parent
+CSRC = PKG / "csrc"
+INCLUDE = REPO / "include"
+LIB = PKG / "libcie_attention.so"
+OPS = PKG / "_cie_torch_ops.so"
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def _nvcc() -> str:
+    home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    cand = Path(home) / "bin" / "nvcc"
+    return str(cand) if cand.exists() else "nvcc"
+
+
+def _stale(target: Path, deps) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def _cu_deps():
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + \
+        sorted(INCLUDE.glob("*.h"))
+
+
+def build_lib(force: bool = False, verbose: bool = False) -> Path:
+    if not force and not _stale(LIB, _cu_deps()):
+        return LIB
+    cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--use_fast_math",
+           "-Xcompiler", "-fPIC,-O3", "-shared", "-I", str(INCLUDE), "-I", str(CSRC),
+           "-Xlinker", "--exclude-libs,ALL", "-o", str(LIB) + ".tmp",
+           str(CSRC / "cie_unity.cu")]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    os.replace(str(LIB) + ".tmp", LIB)
+    return LIB
+
+
+def build_ops(force: bool = False, verbose: bool = False) -> Path:
+    deps = [CSRC / "torch_ops.cpp", INCLUDE / "cie_attention.h", LIB]
+    if not force and not _stale(OPS, deps):
+        return OPS
+    from torch.utils.cpp_extension import load
+    bdir = PKG / "_build"
+    bdir.mkdir(exist_ok=True)
+    load(name="_cie_torch_ops", sources=[str(CSRC / "torch_ops.cpp")],
+         extra_include_paths=[str(INCLUDE)],
+         extra_cflags=["-O3"],
+         # '$$' survives ninja, the single quotes survive the shell: the
+         # runpath is literally $ORIGIN (package dir) and $ORIGIN/.. (from _build)
+         extra_ldflags=[f"-L{PKG}", "-lcie_attention",
+                        "'-Wl,-rpath,$$ORIGIN:$$ORIGIN/..'"],
+         build_directory=str(bdir), with_cuda=True, is_python_module=False,
+         verbose=verbose)
+    shutil.copy2(bdir / "_cie_torch_ops.so", str(OPS) + ".tmp")
+    os.replace(str(OPS) + ".tmp", OPS)
+    return OPS
+
+
+def build_all(force: bool = False, verbose: bool = False) -> None:
+    build_lib(force=force, verbose=verbose)
+    build_ops(force=force, verbose=verbose)
+
+
+if __name__ == "__main__":
+    build_all(force="--force" in sys.argv, verbose="-v" in sys.argv)

@@ -1,0 +1,84 @@
+"""Thin Python callers of the C ABI (``include/cie_attention.h``) on torch tensors.
+
+These are what a ctypes binding of the library looks like: every call passes
+raw device pointers, sizes and element strides, and runs on the given stream
+(default: torch's current stream). Used by the parity tests and by the
+benchmark's end-to-end leg; the torch ops in ``attn.core`` reach the same
+entry points through ``_cie_torch_ops.so``.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import native
+
+
+def _p(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def decode_workspace_bytes(batch: int, num_q_heads: int, head_dim: int, num_splits: int) -> int:
+    return int(native.lib().cie_decode_workspace_bytes(batch, num_q_heads, head_dim, num_splits))
+
+
+def decode_default_splits(batch: int, device: int = 0) -> int:
+    return int(native.lib().cie_decode_default_splits(batch, device))
+
+
+def decode_attention(q, k, v, lens, slot_ids, block_table, out=None, num_splits: int = 0,
+                     workspace: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """cie_decode_attention on (1, B, H_q, D) q and (n_pages, H_kv, 16, D) pools."""
+    B = slot_ids.shape[0]
+    hq, d = q.shape[2], q.shape[3]
+    S = num_splits if num_splits > 0 else decode_default_splits(B, q.device.index or 0)
+    if out is None:
+        out = torch.empty_like(q)
+    need = decode_workspace_bytes(B, hq, d, S)
+    if need > 0 and workspace is None:
+        workspace = torch.empty(need // 4, dtype=torch.float32, device=q.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    st = native.lib().cie_decode_attention(
+        _p(q), _p(k), _p(v), _p(lens), _p(slot_ids), _p(block_table), _p(out), _p(workspace),
+        ws_bytes, B, hq, k.shape[1], d, k.shape[2], k.shape[0], block_table.shape[0],
+        block_table.stride(0), k.stride(0), k.stride(1), S, native.stream_ptr(stream))
+    native.check(st, "cie_decode_attention")
+    return out
+
+
+def mixed_attention(q, k, v, max_seqlen: int, cu_seqlens, kv_lens, slot_ids, block_table,
+                    out=None, stream=None) -> torch.Tensor:
+    """cie_mixed_attention; rows outside every sequence are left as they were in ``out``."""
+    B = slot_ids.shape[0]
+    if out is None:
+        out = torch.empty_like(q)
+    st = native.lib().cie_mixed_attention(
+        _p(q), _p(k), _p(v), int(max_seqlen), _p(cu_seqlens), _p(kv_lens), _p(slot_ids),
+        _p(block_table), _p(out), B, q.shape[1], q.shape[2], k.shape[1], q.shape[3], k.shape[2],
+        k.shape[0], block_table.shape[0], block_table.stride(0), k.stride(0), k.stride(1),
+        native.stream_ptr(stream))
+    native.check(st, "cie_mixed_attention")
+    return out
+
+
+def kv_decode_update(k_cache, v_cache, lens, slot_ids, block_table, k_new, v_new,
+                     stream=None) -> None:
+    """cie_kv_decode_update; ``lens`` is the per-slot length tensor (n_slots,)."""
+    st = native.lib().cie_kv_decode_update(
+        _p(k_cache), _p(v_cache), _p(lens), _p(slot_ids), _p(block_table), _p(k_new), _p(v_new),
+        slot_ids.shape[0], k_cache.shape[1], k_cache.shape[3], k_cache.shape[2],
+        k_cache.shape[0], min(lens.shape[0], block_table.shape[0]), block_table.stride(0),
+        k_cache.stride(0), k_cache.stride(1), k_new.stride(1), k_new.stride(2), v_new.stride(1),
+        v_new.stride(2), native.stream_ptr(stream))
+    native.check(st, "cie_kv_decode_update")
+
+
+def kv_mixed_update(k_cache, v_cache, pages, offsets, k_new, v_new, stream=None) -> None:
+    """cie_kv_mixed_update: token t -> (pages[t], offsets[t])."""
+    st = native.lib().cie_kv_mixed_update(
+        _p(k_cache), _p(v_cache), _p(pages), _p(offsets), _p(k_new), _p(v_new), pages.shape[0],
+        k_cache.shape[1], k_cache.shape[3], k_cache.shape[2], k_cache.shape[0],
+        k_cache.stride(0), k_cache.stride(1), k_new.stride(1), k_new.stride(2), v_new.stride(1),
+        v_new.stride(2), native.stream_ptr(stream))
+    native.check(st, "cie_kv_mixed_update")

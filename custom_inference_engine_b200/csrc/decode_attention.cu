@@ -1,0 +1,537 @@
+// Split-KV paged GQA decode attention for sm_100a.
+//
+// Replaces the reference's decode_gqa_attention_kernel_load / _merge
+// (kernels/decode_attention.py:12-272) behind the same host contract
+// (attn/core.py:13-66).
+//
+// Design (B200-first):
+//  * one CTA per (split, sequence) covers ALL kv heads of that sequence, so a
+//    page is fetched as one 4 KiB TMA box per pool (both heads of
+//    (page, :, 16, 64) are contiguous) into a deep ring of 128B-swizzled
+//    shared-memory stages; a single producer warp reads the int64 block table
+//    32 entries at a time and keeps every stage in flight;
+//  * compute is tiny next to the bytes moved, so each consumer warp uses
+//    warp-level MMA with the GQA group on the MMA's N side: S^T = K . Q^T
+//    (M = 16 keys of a page, N = 8 >= 7 query heads, K = 64 dims) and
+//    O^T += V^T . P^T; P^T is turned into the next B fragment with
+//    movmatrix, so nothing goes back through shared memory;
+//  * two consumer warps per kv head take alternate pages and are merged at
+//    the end; with more than one split per sequence each CTA writes an
+//    (m, l, acc) partial and a small merge kernel combines them.
+// Numerics follow the reference: fp16 dot with fp32 accumulation, scale
+// after the dot, fp32 online softmax, probabilities rounded to fp16 before
+// P.V, one fp16 rounding of the output.
+#include <math_constants.h>
+
+#include "cie_common.cuh"
+#include "cie_host.h"
+
+namespace cie {
+namespace decode {
+
+constexpr int kD = 64;
+constexpr int kPage = 16;
+constexpr int kGroup = 7;
+constexpr int kHeadTileBytes = kPage * kD * 2;  // 2 KiB: one head of one page
+
+template <int HKV>
+struct Cfg {
+  static constexpr int kConsumerWarps = 2 * HKV;
+  static constexpr int kThreads = 32 * (1 + kConsumerWarps);
+  static constexpr int kStageBytes = 2 * HKV * kHeadTileBytes;  // K + V
+  static constexpr int kStages = HKV == 1 ? 16 : (HKV == 2 ? 12 : 6);
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  // merge scratch per kv head: m[8], l[8], acc[64][8] fp32
+  static constexpr int kScratchFloats = 8 + 8 + kD * 8;
+  static constexpr int kScratchBytes = HKV * kScratchFloats * 4;
+  static constexpr int kBarBytes = 2 * kStages * 8;
+  static constexpr int kSmemBytes = 1024 + kRingBytes + kScratchBytes + kBarBytes;
+};
+
+struct Params {
+  const __half* q;            // (B, H_q, D)
+  const int64_t* lens;        // (B,)
+  const int64_t* slot_ids;    // (B,)
+  const int64_t* block_table; // (n_slots, bt_stride)
+  __half* o;                  // (B, H_q, D)
+  float* ws_acc;              // (B, S, H_q, D)
+  float* ws_ml;               // (B, S, H_q, 2)
+  int batch;
+  int num_splits;
+  int64_t n_pages;
+  int64_t n_slots;
+  int64_t bt_stride;
+};
+
+__device__ __forceinline__ float shfl_max_group(float x) {
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 16));
+  return x;
+}
+__device__ __forceinline__ float shfl_sum_group(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 4);
+  x += __shfl_xor_sync(0xffffffffu, x, 8);
+  x += __shfl_xor_sync(0xffffffffu, x, 16);
+  return x;
+}
+
+template <int HKV>
+__global__ void __launch_bounds__(Cfg<HKV>::kThreads)
+    decode_split_kernel(const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  using C = Cfg<HKV>;
+  constexpr int H_Q = HKV * kGroup;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  float* scratch = reinterpret_cast<float*>(smem + C::kRingBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kRingBytes + C::kScratchBytes);
+  const uint32_t ring_u32 = smem_u32(ring);
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + 8u * C::kStages;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int split = blockIdx.x;
+  const int b = blockIdx.y;
+  const int S = p.num_splits;
+
+  // ---- per-sequence page range of this split -------------------------------
+  int64_t slot = p.slot_ids[b];
+  int64_t L = p.lens[b];
+  bool bad = false;
+  if (slot < 0 || slot >= p.n_slots) {
+    if (threadIdx.x == 0) raise_error(CIE_DEVERR_BAD_SLOT);
+    bad = true;
+  }
+  if (L < 0) L = 0;
+  if (!bad && (L + kPage - 1) / kPage > p.bt_stride) {
+    if (threadIdx.x == 0) raise_error(CIE_DEVERR_BAD_LENGTH);
+    L = p.bt_stride * kPage;
+  }
+  if (bad) L = 0;
+  const int n_seq_pages = static_cast<int>((L + kPage - 1) / kPage);
+  const int pps = (n_seq_pages + S - 1) / S;
+  const int page_begin = split * pps;
+  const int n = max(0, min(page_begin + pps, n_seq_pages) - page_begin);
+  const int Li = static_cast<int>(L);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, HKV);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ======================= producer warp ==================================
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+    }
+    const int64_t* bt_row = p.block_table + slot * p.bt_stride + page_begin;
+    bool abort = false;
+    int issued = 0;
+    for (int base = 0; base < n && !abort; base += 32) {
+      int page = 0;
+      if (base + lane < n) {
+        int64_t pid = bt_row[base + lane];
+        if (pid < 0 || pid >= p.n_pages) {
+          raise_error(CIE_DEVERR_BAD_PAGE);
+          pid = 0;
+        }
+        page = static_cast<int>(pid);
+      }
+      const int cnt = min(32, n - base);
+      for (int t = 0; t < cnt; ++t) {
+        const int pg = __shfl_sync(0xffffffffu, page, t);
+        if (lane == 0) {
+          const int i = base + t;
+          const int s = i % C::kStages;
+          const uint32_t use = static_cast<uint32_t>(i / C::kStages);
+          if (i >= C::kStages && !mbar_wait(empty0 + 8u * s, (use & 1u) ^ 1u, CIE_DEVERR_WAIT_TIMEOUT))
+            abort = true;
+          if (!abort) {
+            const uint32_t dst = ring_u32 + s * C::kStageBytes;
+            mbar_arrive_expect_tx(full0 + 8u * s, C::kStageBytes);
+            tma_load_4d(dst, &tm_k, full0 + 8u * s, 0, 0, 0, pg);
+            tma_load_4d(dst + HKV * kHeadTileBytes, &tm_v, full0 + 8u * s, 0, 0, 0, pg);
+            ++issued;
+          }
+        }
+        abort = __shfl_sync(0xffffffffu, abort ? 1 : 0, 0) != 0;
+        if (abort) break;
+      }
+    }
+    // Never leave the CTA with bulk copies in flight: wait (bounded) for the
+    // last load issued into every stage.
+    if (lane == 0) {
+      for (int i = max(0, issued - C::kStages); i < issued; ++i) {
+        const int s = i % C::kStages;
+        mbar_wait(full0 + 8u * s, static_cast<uint32_t>(i / C::kStages) & 1u,
+                  CIE_DEVERR_WAIT_TIMEOUT);
+      }
+    }
+    return;
+  }
+
+  // ========================= consumer warps ===================================
+  const int cw = warp - 1;
+  const int h = cw % HKV;        // kv head
+  const int par = cw / HKV;      // page parity handled by this warp
+  const int g = lane >> 2;       // fragment row group: query head within the group
+  const int t4 = lane & 3;
+
+  // Q^T as the B operand: b0 = Q[g][16ks + 2t4 .. +1], b1 = Q[g][16ks + 8 + 2t4 .. +1]
+  uint32_t bq[4][2];
+  {
+    const bool valid = g < kGroup;
+    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+        p.q + (static_cast<int64_t>(b) * H_Q + h * kGroup + (valid ? g : 0)) * kD);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      bq[ks][0] = valid ? qrow[(ks * 16 + 2 * t4) >> 1] : 0u;
+      bq[ks][1] = valid ? qrow[(ks * 16 + 8 + 2 * t4) >> 1] : 0u;
+    }
+  }
+
+  constexpr float kScale = 0.125f;  // head_dim ** -0.5 for D = 64
+  float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F;  // heads 2*t4, 2*t4+1
+  float l0 = 0.f, l1 = 0.f;                      // per-thread partial sums
+  float acc[4][4];
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[mt][e] = 0.f;
+
+  for (int i = par; i < n; i += 2) {
+    const int s = i % C::kStages;
+    const uint32_t use = static_cast<uint32_t>(i / C::kStages);
+    if (!mbar_wait(full0 + 8u * s, use & 1u, CIE_DEVERR_WAIT_TIMEOUT)) break;
+    // Head h's 16 rows start at a multiple of 1 KiB inside the stage, so the
+    // 128B-swizzle phase of row r is r mod 8.
+    const uint32_t kt = ring_u32 + s * C::kStageBytes + h * kHeadTileBytes;
+    const uint32_t vt = kt + HKV * kHeadTileBytes;
+
+    // S^T (16 keys x 8 heads) = K (16 x 64) . Q^T (64 x 8)
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      ldmatrix_x4(kt + sw128(lane & 15, ks * 2 + (lane >> 4)), a0, a1, a2, a3);
+      mma_16816(sc, a0, a1, a2, a3, bq[ks][0], bq[ks][1]);
+    }
+    const int key0 = (page_begin + i) * kPage + g;
+    const int key1 = key0 + 8;
+    const float s0 = key0 < Li ? sc[0] * kScale : -CUDART_INF_F;
+    const float s1 = key0 < Li ? sc[1] * kScale : -CUDART_INF_F;
+    const float s2 = key1 < Li ? sc[2] * kScale : -CUDART_INF_F;
+    const float s3 = key1 < Li ? sc[3] * kScale : -CUDART_INF_F;
+    const float mx0 = shfl_max_group(fmaxf(s0, s2));
+    const float mx1 = shfl_max_group(fmaxf(s1, s3));
+    const float mn0 = fmaxf(m0, mx0);
+    const float mn1 = fmaxf(m1, mx1);
+    // every visited page holds at least one visible key, so mn* is finite
+    const float al0 = ex2((m0 - mn0) * kLog2e);
+    const float al1 = ex2((m1 - mn1) * kLog2e);
+    const float p0 = ex2((s0 - mn0) * kLog2e);
+    const float p1 = ex2((s1 - mn1) * kLog2e);
+    const float p2 = ex2((s2 - mn0) * kLog2e);
+    const float p3 = ex2((s3 - mn1) * kLog2e);
+    l0 = l0 * al0 + (p0 + p2);
+    l1 = l1 * al1 + (p1 + p3);
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      acc[mt][0] *= al0;
+      acc[mt][1] *= al1;
+      acc[mt][2] *= al0;
+      acc[mt][3] *= al1;
+    }
+    const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));
+    const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));
+
+    // Rows past the sequence end hold stale pool data; zero them so that
+    // 0 * (non-finite) cannot reach the accumulator (the reference loads
+    // them masked with other=0).
+    const int valid_rows = Li - (page_begin + i) * kPage;
+    if (valid_rows < kPage) {
+      for (int e = lane; e < (kPage - valid_rows) * 8; e += 32) {
+        const int r = valid_rows + (e >> 3);
+        const uint32_t addr = vt + sw128(r, e & 7);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0) : "memory");
+      }
+      __syncwarp();
+    }
+
+    // O^T (64 dims x 8 heads) += V^T (64 x 16 keys) . P^T (16 x 8)
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      uint32_t a0, a1, a2, a3;
+      const int key = (lane & 7) + ((lane >> 4) << 3);
+      ldmatrix_x4_trans(vt + sw128(key, mt * 2 + ((lane >> 3) & 1)), a0, a1, a2, a3);
+      mma_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+    }
+    if (valid_rows < kPage) fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8u * s);
+  }
+
+  l0 = shfl_sum_group(l0);
+  l1 = shfl_sum_group(l1);
+
+  // ---- merge the two page-parity warps of kv head h -------------------------
+  float* sc_h = scratch + h * C::kScratchFloats;  // m[8] | l[8] | acc[64][8]
+  if (par == 1) {
+    if (g == 0) {
+      sc_h[2 * t4] = m0;
+      sc_h[2 * t4 + 1] = m1;
+      sc_h[8 + 2 * t4] = l0;
+      sc_h[8 + 2 * t4 + 1] = l1;
+    }
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      const int d0 = mt * 16 + g;
+      sc_h[16 + d0 * 8 + 2 * t4] = acc[mt][0];
+      sc_h[16 + d0 * 8 + 2 * t4 + 1] = acc[mt][1];
+      sc_h[16 + (d0 + 8) * 8 + 2 * t4] = acc[mt][2];
+      sc_h[16 + (d0 + 8) * 8 + 2 * t4 + 1] = acc[mt][3];
+    }
+  }
+  // named barrier per kv head: its two consumer warps (64 threads)
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + h) : "memory");
+  if (par == 1) return;
+
+  {
+    const float mb0 = sc_h[2 * t4], mb1 = sc_h[2 * t4 + 1];
+    const float lb0 = sc_h[8 + 2 * t4], lb1 = sc_h[8 + 2 * t4 + 1];
+    const float M0 = fmaxf(m0, mb0), M1 = fmaxf(m1, mb1);
+    const float wa0 = M0 == -CUDART_INF_F ? 0.f : ex2((m0 - M0) * kLog2e);
+    const float wb0 = M0 == -CUDART_INF_F ? 0.f : ex2((mb0 - M0) * kLog2e);
+    const float wa1 = M1 == -CUDART_INF_F ? 0.f : ex2((m1 - M1) * kLog2e);
+    const float wb1 = M1 == -CUDART_INF_F ? 0.f : ex2((mb1 - M1) * kLog2e);
+    l0 = l0 * wa0 + lb0 * wb0;
+    l1 = l1 * wa1 + lb1 * wb1;
+    m0 = M0;
+    m1 = M1;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      const int d0 = mt * 16 + g;
+      acc[mt][0] = acc[mt][0] * wa0 + sc_h[16 + d0 * 8 + 2 * t4] * wb0;
+      acc[mt][1] = acc[mt][1] * wa1 + sc_h[16 + d0 * 8 + 2 * t4 + 1] * wb1;
+      acc[mt][2] = acc[mt][2] * wa0 + sc_h[16 + (d0 + 8) * 8 + 2 * t4] * wb0;
+      acc[mt][3] = acc[mt][3] * wa1 + sc_h[16 + (d0 + 8) * 8 + 2 * t4 + 1] * wb1;
+    }
+  }
+  __syncwarp();
+
+  const int hq0 = h * kGroup + 2 * t4;  // global q head of acc[.][0] / acc[.][2]
+  if (S == 1) {
+    // final output: acc / l; a row that saw no key (L == 0) is zero
+    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+    const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+    // stage fp16 rows in the (now free) scratch area, then write 16-byte chunks
+    __half* stage = reinterpret_cast<__half*>(sc_h);  // [7][64]
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      const int d0 = mt * 16 + g;
+      if (2 * t4 < kGroup) {
+        stage[(2 * t4) * kD + d0] = __float2half_rn(acc[mt][0] * inv0);
+        stage[(2 * t4) * kD + d0 + 8] = __float2half_rn(acc[mt][2] * inv0);
+      }
+      if (2 * t4 + 1 < kGroup) {
+        stage[(2 * t4 + 1) * kD + d0] = __float2half_rn(acc[mt][1] * inv1);
+        stage[(2 * t4 + 1) * kD + d0 + 8] = __float2half_rn(acc[mt][3] * inv1);
+      }
+    }
+    __syncwarp();
+    const uint4* src = reinterpret_cast<const uint4*>(stage);
+    uint4* dst = reinterpret_cast<uint4*>(p.o + (static_cast<int64_t>(b) * H_Q + h * kGroup) * kD);
+    for (int e = lane; e < kGroup * kD / 8; e += 32) dst[e] = src[e];
+  } else {
+    const int64_t base = (static_cast<int64_t>(b) * S + split) * H_Q;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int hq = hq0 + hh;
+      if (2 * t4 + hh >= kGroup) continue;
+      float* a = p.ws_acc + (base + hq) * kD;
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        a[mt * 16 + g] = acc[mt][hh];
+        a[mt * 16 + g + 8] = acc[mt][2 + hh];
+      }
+      if (g == 0) {
+        p.ws_ml[(base + hq) * 2 + 0] = hh ? m1 : m0;
+        p.ws_ml[(base + hq) * 2 + 1] = hh ? l1 : l0;
+      }
+    }
+  }
+}
+
+// Combines the split partials of one sequence: O = sum_s w_s acc_s / sum_s w_s l_s,
+// w_s = exp(m_s - max m); splits that saw no key (m = -inf) are skipped and a
+// sequence with no key at all gets a zero row (reference merge,
+// kernels/decode_attention.py:243-264).
+__global__ void __launch_bounds__(256)
+    decode_merge_kernel(const float* __restrict__ ws_acc, const float* __restrict__ ws_ml,
+                        __half* __restrict__ o, int num_splits, int num_q_heads) {
+  const int b = blockIdx.x;
+  const int S = num_splits;
+  for (int idx = threadIdx.x; idx < num_q_heads * (kD / 2); idx += blockDim.x) {
+    const int hq = idx / (kD / 2);
+    const int d = (idx % (kD / 2)) * 2;
+    const int64_t base = static_cast<int64_t>(b) * S * num_q_heads;
+    float M = -CUDART_INF_F;
+    for (int s = 0; s < S; ++s) M = fmaxf(M, ws_ml[((base + s * num_q_heads) + hq) * 2]);
+    float den = 0.f, n0 = 0.f, n1 = 0.f;
+    if (M != -CUDART_INF_F) {
+      for (int s = 0; s < S; ++s) {
+        const int64_t r = base + s * num_q_heads + hq;
+        const float m = ws_ml[r * 2];
+        if (m == -CUDART_INF_F) continue;
+        const float w = ex2((m - M) * kLog2e);
+        den += w * ws_ml[r * 2 + 1];
+        const float2 a = *reinterpret_cast<const float2*>(ws_acc + r * kD + d);
+        n0 += w * a.x;
+        n1 += w * a.y;
+      }
+    }
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    *reinterpret_cast<__half2*>(o + (static_cast<int64_t>(b) * num_q_heads + hq) * kD + d) =
+        __floats2half2_rn(n0 * inv, n1 * inv);
+  }
+}
+
+template <int HKV>
+int launch(const void* q, const void* k, const void* v, const int64_t* lens,
+           const int64_t* slot_ids, const int64_t* block_table, void* o, float* ws, int batch,
+           int64_t n_pages, int64_t n_slots, int64_t bt_stride, int64_t page_stride,
+           int64_t head_stride, int S, cudaStream_t stream) {
+  using C = Cfg<HKV>;
+  CUtensorMap tm_k, tm_v;
+  const uint64_t dims[4] = {kD, kPage, HKV, static_cast<uint64_t>(n_pages)};
+  const uint64_t strides[3] = {kD * 2, static_cast<uint64_t>(head_stride) * 2,
+                               static_cast<uint64_t>(page_stride) * 2};
+  const uint32_t box[4] = {kD, kPage, HKV, 1};
+  int st = encode_tensor_map(&tm_k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(k), dims,
+                             strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != CIE_OK) return st;
+  st = encode_tensor_map(&tm_v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(v), dims,
+                         strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != CIE_OK) return st;
+  st = ensure_smem_attribute(reinterpret_cast<const void*>(&decode_split_kernel<HKV>), C::kSmemBytes,
+                             HKV);
+  if (st != CIE_OK) return st;
+
+  Params p;
+  p.q = static_cast<const __half*>(q);
+  p.lens = lens;
+  p.slot_ids = slot_ids;
+  p.block_table = block_table;
+  p.o = static_cast<__half*>(o);
+  const int H_Q = HKV * kGroup;
+  p.ws_acc = ws;
+  p.ws_ml = ws == nullptr ? nullptr : ws + static_cast<int64_t>(batch) * S * H_Q * kD;
+  p.batch = batch;
+  p.num_splits = S;
+  p.n_pages = n_pages;
+  p.n_slots = n_slots;
+  p.bt_stride = bt_stride;
+  dim3 grid(S, batch);
+  decode_split_kernel<HKV><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tm_k, tm_v, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
+  if (S > 1) {
+    decode_merge_kernel<<<batch, 256, 0, stream>>>(p.ws_acc, p.ws_ml, p.o, S, H_Q);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
+  }
+  return CIE_OK;
+}
+
+}  // namespace decode
+}  // namespace cie
+
+extern "C" {
+
+int cie_decode_default_splits(int batch, int device) {
+  int sms = 148;
+  if (device >= 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && n > 0)
+      sms = n;
+  }
+  if (batch <= 0) return 1;
+  // two resident CTAs per SM; one wave of (split, sequence) CTAs
+  int s = (2 * sms) / batch;
+  if (s < 1) s = 1;
+  if (s > 256) s = 256;
+  return s;
+}
+
+size_t cie_decode_workspace_bytes(int batch, int num_q_heads, int head_dim, int num_splits) {
+  if (batch <= 0 || num_splits <= 1 || num_q_heads <= 0 || head_dim <= 0) return 0;
+  const size_t rows = static_cast<size_t>(batch) * num_splits * num_q_heads;
+  return rows * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
+}
+
+int cie_decode_attention(const void* q, const void* k, const void* v, const int64_t* lens,
+                         const int64_t* slot_ids, const int64_t* block_table, void* o,
+                         void* workspace, size_t workspace_bytes, int batch, int num_q_heads,
+                         int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
+                         int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
+                         int64_t kv_head_stride, int num_splits, cie_stream_t stream) {
+  using namespace cie;
+  if (batch < 0) return fail(CIE_ERR_INVALID_ARGUMENT, "batch < 0");
+  if (batch == 0) return CIE_OK;
+  if (!q || !k || !v || !lens || !slot_ids || !block_table || !o)
+    return fail(CIE_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (head_dim != decode::kD || page_size != decode::kPage)
+    return fail(CIE_ERR_UNSUPPORTED, "head_dim %d / page_size %d (supported: 64 / 16)", head_dim,
+                page_size);
+  if (num_kv_heads != 1 && num_kv_heads != 2 && num_kv_heads != 4)
+    return fail(CIE_ERR_UNSUPPORTED, "num_kv_heads %d (supported: 1, 2, 4)", num_kv_heads);
+  if (num_q_heads != num_kv_heads * decode::kGroup)
+    return fail(CIE_ERR_UNSUPPORTED, "num_q_heads %d must be 7 * num_kv_heads", num_q_heads);
+  if (n_pages < 1 || n_slots < 1 || bt_stride < 1)
+    return fail(CIE_ERR_INVALID_ARGUMENT, "n_pages / n_slots / bt_stride must be >= 1");
+  if (n_pages >= (int64_t(1) << 31))
+    return fail(CIE_ERR_OVERFLOW, "n_pages %lld does not fit int32", (long long)n_pages);
+  if (batch > 65535) return fail(CIE_ERR_UNSUPPORTED, "batch %d > 65535", batch);
+  if (kv_head_stride < page_size * head_dim || kv_page_stride < kv_head_stride * num_kv_heads)
+    return fail(CIE_ERR_INVALID_ARGUMENT, "overlapping K/V strides (page %lld, head %lld)",
+                (long long)kv_page_stride, (long long)kv_head_stride);
+  if ((kv_page_stride % 8) || (kv_head_stride % 8) || !aligned16(k) || !aligned16(v) ||
+      !aligned16(q) || !aligned16(o))
+    return fail(CIE_ERR_ALIGNMENT, "q/o/k/v must be 16-byte aligned with 16-byte strides");
+  int S = num_splits > 0 ? num_splits : cie_decode_default_splits(batch, current_device());
+  if (S > 4096) return fail(CIE_ERR_INVALID_ARGUMENT, "num_splits %d > 4096", S);
+  float* ws = nullptr;
+  if (S > 1) {
+    const size_t need = cie_decode_workspace_bytes(batch, num_q_heads, head_dim, S);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(CIE_ERR_WORKSPACE, "split path needs %zu workspace bytes, got %zu", need,
+                  workspace == nullptr ? size_t(0) : workspace_bytes);
+    if (!aligned16(workspace)) return fail(CIE_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+    ws = static_cast<float*>(workspace);
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (num_kv_heads) {
+    case 1:
+      return decode::launch<1>(q, k, v, lens, slot_ids, block_table, o, ws, batch, n_pages, n_slots,
+                               bt_stride, kv_page_stride, kv_head_stride, S, s);
+    case 2:
+      return decode::launch<2>(q, k, v, lens, slot_ids, block_table, o, ws, batch, n_pages, n_slots,
+                               bt_stride, kv_page_stride, kv_head_stride, S, s);
+    default:
+      return decode::launch<4>(q, k, v, lens, slot_ids, block_table, o, ws, batch, n_pages, n_slots,
+                               bt_stride, kv_page_stride, kv_head_stride, S, s);
+  }
+}
+
+}  // extern "C"

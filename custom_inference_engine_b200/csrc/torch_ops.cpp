@@ -1,0 +1,211 @@
+// Torch custom ops over the C ABI of libcie_attention.so.
+//
+// Schemas match the reference's triton_op registrations (attn/core.py:119-137)
+// so callers, Dynamo graphs and the piecewise splitter (which matches
+// torch.ops.inference.gqa_mixed_attention.default and reads its kv_lens
+// kwarg) see the same ops. Checks mirror the reference host asserts
+// (attn/core.py:18-34, 76-86) and raise RuntimeError. Outputs and the split
+// workspace come from the caching allocator, so the ops are safe inside CUDA
+// graph capture; nothing here synchronises with the host.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include "cie_attention.h"
+
+namespace {
+
+void check_status(int st, const char* what) {
+  TORCH_CHECK(st == CIE_OK, what, ": ", cie_status_string(st), ": ", cie_last_error_message());
+}
+
+void check_i64(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.scalar_type() == at::kLong, name, " must be int64");
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+
+void check_kv_pool(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v) {
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(), "q, k, v must be CUDA tensors");
+  TORCH_CHECK(q.scalar_type() == at::kHalf && k.scalar_type() == at::kHalf &&
+                  v.scalar_type() == at::kHalf,
+              "q, k, v must be float16");
+  TORCH_CHECK(q.dim() == 4 && q.size(0) == 1, "q must be (1, T, H_q, D)");
+  TORCH_CHECK(k.dim() == 4, "k must be (n_pages, H_kv, page_size, D)");
+  TORCH_CHECK(k.sizes() == v.sizes(), "k and v shapes differ");
+  TORCH_CHECK(q.size(2) % k.size(1) == 0, "H_q must be a multiple of H_kv");
+  TORCH_CHECK(k.size(3) == q.size(3), "head_dim mismatch between q and k");
+  TORCH_CHECK(q.is_contiguous(), "q must be contiguous");
+  TORCH_CHECK(k.strides() == v.strides() && k.stride(3) == 1 && k.stride(2) == k.size(3),
+              "k and v must share strides with unit inner stride and row stride head_dim");
+}
+
+at::Tensor decode_impl(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                       const at::Tensor& lens, const at::Tensor& slot_ids,
+                       const at::Tensor& block_table, int64_t num_splits) {
+  check_kv_pool(q, k, v);
+  check_i64(lens, "lens");
+  check_i64(slot_ids, "slot_ids");
+  check_i64(block_table, "block_table");
+  const int64_t B = slot_ids.size(0);
+  TORCH_CHECK(lens.dim() == 1 && lens.size(0) == B, "lens must be (B,)");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.size(1) == k.size(0),
+              "block_table must be (n_slots, n_pages)");
+  TORCH_CHECK(block_table.stride(1) == 1, "block_table rows must be contiguous");
+  TORCH_CHECK(q.size(1) == B, "q must hold one token per sequence");
+  TORCH_CHECK(lens.is_contiguous() && slot_ids.is_contiguous(), "lens / slot_ids must be contiguous");
+  c10::cuda::CUDAGuard guard(q.device());
+  at::Tensor o = at::empty_like(q);
+  if (B == 0) return o;
+  int S = static_cast<int>(num_splits);
+  if (S <= 0) S = cie_decode_default_splits(static_cast<int>(B), q.get_device());
+  const size_t ws_bytes =
+      cie_decode_workspace_bytes(static_cast<int>(B), static_cast<int>(q.size(2)),
+                                 static_cast<int>(q.size(3)), S);
+  at::Tensor ws;
+  if (ws_bytes > 0)
+    ws = at::empty({static_cast<int64_t>(ws_bytes / sizeof(float))},
+                   q.options().dtype(at::kFloat));
+  const int st = cie_decode_attention(
+      q.data_ptr(), k.data_ptr(), v.data_ptr(), lens.data_ptr<int64_t>(),
+      slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(), o.data_ptr(),
+      ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, static_cast<int>(B),
+      static_cast<int>(q.size(2)), static_cast<int>(k.size(1)), static_cast<int>(q.size(3)),
+      static_cast<int>(k.size(2)), k.size(0), block_table.size(0), block_table.stride(0),
+      k.stride(0), k.stride(1), S,
+      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "gqa_decode_attention");
+  return o;
+}
+
+at::Tensor gqa_decode_attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                const at::Tensor& lens, const at::Tensor& slot_ids,
+                                const at::Tensor& block_table) {
+  return decode_impl(q, k, v, lens, slot_ids, block_table, 0);
+}
+
+at::Tensor gqa_decode_attention_splits(const at::Tensor& q, const at::Tensor& k,
+                                       const at::Tensor& v, const at::Tensor& lens,
+                                       const at::Tensor& slot_ids, const at::Tensor& block_table,
+                                       int64_t num_splits) {
+  return decode_impl(q, k, v, lens, slot_ids, block_table, num_splits);
+}
+
+at::Tensor gqa_mixed_attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                               c10::SymInt max_seqlen_sym, const at::Tensor& cu_seqlens,
+                               const at::Tensor& kv_lens, const at::Tensor& slot_ids,
+                               const at::Tensor& block_table) {
+  const int64_t max_seqlen = max_seqlen_sym.expect_int();
+  check_kv_pool(q, k, v);
+  TORCH_CHECK(k.is_contiguous() && v.is_contiguous(), "k and v must be contiguous");
+  check_i64(cu_seqlens, "cu_seqlens");
+  check_i64(kv_lens, "kv_lens");
+  check_i64(slot_ids, "slot_ids");
+  check_i64(block_table, "block_table");
+  const int64_t B = slot_ids.size(0);
+  TORCH_CHECK(kv_lens.dim() == 1 && kv_lens.size(0) == B, "kv_lens must be (B,)");
+  TORCH_CHECK(cu_seqlens.dim() == 1 && cu_seqlens.size(0) == B + 1, "cu_seqlens must be (B+1,)");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.size(1) == k.size(0),
+              "block_table must be (n_slots, n_pages)");
+  TORCH_CHECK(block_table.stride(1) == 1, "block_table rows must be contiguous");
+  TORCH_CHECK(cu_seqlens.is_contiguous() && kv_lens.is_contiguous() && slot_ids.is_contiguous(),
+              "cu_seqlens / kv_lens / slot_ids must be contiguous");
+  c10::cuda::CUDAGuard guard(q.device());
+  at::Tensor o = at::empty_like(q);
+  const int st = cie_mixed_attention(
+      q.data_ptr(), k.data_ptr(), v.data_ptr(), max_seqlen, cu_seqlens.data_ptr<int64_t>(),
+      kv_lens.data_ptr<int64_t>(), slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(),
+      o.data_ptr(), static_cast<int>(B), q.size(1), static_cast<int>(q.size(2)),
+      static_cast<int>(k.size(1)), static_cast<int>(q.size(3)), static_cast<int>(k.size(2)),
+      k.size(0), block_table.size(0), block_table.stride(0), k.stride(0), k.stride(1),
+      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "gqa_mixed_attention");
+  return o;
+}
+
+void check_update_src(const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& kn,
+                      const at::Tensor& vn) {
+  TORCH_CHECK(kc.is_cuda() && vc.is_cuda() && kn.is_cuda() && vn.is_cuda(),
+              "caches and new rows must be CUDA tensors");
+  TORCH_CHECK(kc.scalar_type() == at::kHalf && vc.scalar_type() == at::kHalf &&
+                  kn.scalar_type() == at::kHalf && vn.scalar_type() == at::kHalf,
+              "caches and new rows must be float16");
+  TORCH_CHECK(kc.dim() == 4 && kc.sizes() == vc.sizes() && kc.strides() == vc.strides(),
+              "k_cache / v_cache must be (n_pages, H_kv, page_size, D) with equal strides");
+  TORCH_CHECK(kc.stride(3) == 1 && kc.stride(2) == kc.size(3), "cache rows must be dense");
+  TORCH_CHECK(kn.dim() == 4 && kn.size(0) == 1 && kn.size(2) == kc.size(1) &&
+                  kn.size(3) == kc.size(3) && kn.sizes() == vn.sizes(),
+              "new rows must be (1, T, H_kv, D)");
+  TORCH_CHECK(kn.stride(3) == 1 && vn.stride(3) == 1, "new rows need unit inner stride");
+}
+
+void kv_decode_update(at::Tensor& k_cache, at::Tensor& v_cache, const at::Tensor& lens,
+                      const at::Tensor& slot_ids, const at::Tensor& block_table,
+                      const at::Tensor& k_new, const at::Tensor& v_new) {
+  check_update_src(k_cache, v_cache, k_new, v_new);
+  check_i64(lens, "lens");
+  check_i64(slot_ids, "slot_ids");
+  check_i64(block_table, "block_table");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.stride(1) == 1, "block_table must be 2-D");
+  TORCH_CHECK(k_new.size(1) == slot_ids.size(0), "one new row per slot id");
+  TORCH_CHECK(lens.is_contiguous() && slot_ids.is_contiguous(), "lens / slot_ids contiguous");
+  c10::cuda::CUDAGuard guard(k_cache.device());
+  const int st = cie_kv_decode_update(
+      k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr<int64_t>(),
+      slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(), k_new.data_ptr(),
+      v_new.data_ptr(), static_cast<int>(slot_ids.size(0)), static_cast<int>(k_cache.size(1)),
+      static_cast<int>(k_cache.size(3)), static_cast<int>(k_cache.size(2)), k_cache.size(0),
+      lens.size(0) < block_table.size(0) ? lens.size(0) : block_table.size(0),
+      block_table.stride(0), k_cache.stride(0), k_cache.stride(1), k_new.stride(1),
+      k_new.stride(2), v_new.stride(1), v_new.stride(2),
+      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "kv_decode_update");
+}
+
+void kv_mixed_update(at::Tensor& k_cache, at::Tensor& v_cache, const at::Tensor& pages,
+                     const at::Tensor& offsets, const at::Tensor& k_new, const at::Tensor& v_new) {
+  check_update_src(k_cache, v_cache, k_new, v_new);
+  check_i64(pages, "pages");
+  check_i64(offsets, "offsets");
+  TORCH_CHECK(pages.dim() == 1 && offsets.dim() == 1 && pages.size(0) == offsets.size(0) &&
+                  pages.size(0) == k_new.size(1),
+              "pages / offsets must be (T,) matching the new rows");
+  TORCH_CHECK(pages.is_contiguous() && offsets.is_contiguous(), "pages / offsets contiguous");
+  c10::cuda::CUDAGuard guard(k_cache.device());
+  const int st = cie_kv_mixed_update(
+      k_cache.data_ptr(), v_cache.data_ptr(), pages.data_ptr<int64_t>(),
+      offsets.data_ptr<int64_t>(), k_new.data_ptr(), v_new.data_ptr(), pages.size(0),
+      static_cast<int>(k_cache.size(1)), static_cast<int>(k_cache.size(3)),
+      static_cast<int>(k_cache.size(2)), k_cache.size(0), k_cache.stride(0), k_cache.stride(1),
+      k_new.stride(1), k_new.stride(2), v_new.stride(1), v_new.stride(2),
+      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "kv_mixed_update");
+}
+
+}  // namespace
+
+TORCH_LIBRARY(inference, m) {
+  m.def(
+      "gqa_decode_attention(Tensor q, Tensor k, Tensor v, Tensor lens, Tensor slot_ids, "
+      "Tensor block_table) -> Tensor");
+  m.def(
+      "gqa_mixed_attention(Tensor q, Tensor k, Tensor v, SymInt max_seqlen, Tensor cu_seqlens, "
+      "Tensor kv_lens, Tensor slot_ids, Tensor block_table) -> Tensor");
+  m.def(
+      "gqa_decode_attention_splits(Tensor q, Tensor k, Tensor v, Tensor lens, Tensor slot_ids, "
+      "Tensor block_table, int num_splits) -> Tensor");
+  m.def(
+      "kv_decode_update(Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor lens, Tensor slot_ids, "
+      "Tensor block_table, Tensor k_new, Tensor v_new) -> ()");
+  m.def(
+      "kv_mixed_update(Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor pages, Tensor offsets, "
+      "Tensor k_new, Tensor v_new) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(inference, CUDA, m) {
+  m.impl("gqa_decode_attention", &gqa_decode_attention);
+  m.impl("gqa_mixed_attention", &gqa_mixed_attention);
+  m.impl("gqa_decode_attention_splits", &gqa_decode_attention_splits);
+  m.impl("kv_decode_update", &kv_decode_update);
+  m.impl("kv_mixed_update", &kv_mixed_update);
+}

@@ -1,0 +1,149 @@
+/*
+ * cie_attention.h -- C ABI of the B200 (sm_100a) paged GQA attention library
+ * (libcie_attention.so).
+ *
+ * Every entry point takes plain device pointers, sizes and strides (in
+ * elements), launches asynchronously on `stream`, performs no host<->device
+ * synchronisation and allocates nothing, so each call can be captured in a
+ * CUDA graph. Return value: CIE_OK or a negative cie_status; on error nothing
+ * was launched and cie_last_error_message() (thread-local) says why.
+ *
+ * Layouts are the reference engine's (eteboun/custom_inference_engine):
+ *   q / o        (1, T, num_q_heads, head_dim)  fp16, contiguous
+ *   k / v pool   (n_pages, num_kv_heads, page_size, head_dim) fp16,
+ *                row stride head_dim, unit inner stride (kv_cache/storage.py:32-48)
+ *   block_table  (n_slots, bt_stride) int64, slot s's logical page j at
+ *                block_table[s * bt_stride + j]   (kv_cache/storage.py:54-56)
+ *   lens, kv_lens, slot_ids, pages, offsets: int64; cu_seqlens: int64 (B+1)
+ * Supported shapes: head_dim 64, page_size 16, num_q_heads / num_kv_heads = 7
+ * (Qwen2.5-0.5B: 14 / 2), num_kv_heads <= 8.
+ */
+#ifndef CIE_ATTENTION_H_
+#define CIE_ATTENTION_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t; declared here so the header needs no CUDA headers. */
+typedef struct CUstream_st* cie_stream_t;
+
+enum cie_status {
+  CIE_OK = 0,
+  CIE_ERR_INVALID_ARGUMENT = -1, /* null pointer, negative size, bad stride   */
+  CIE_ERR_UNSUPPORTED = -2,      /* head_dim / page_size / group not supported */
+  CIE_ERR_OVERFLOW = -3,         /* an index would not fit the kernel's int32  */
+  CIE_ERR_ALIGNMENT = -4,        /* pointer or stride breaks a 16-byte rule    */
+  CIE_ERR_WORKSPACE = -5,        /* workspace missing or too small             */
+  CIE_ERR_CUDA = -6              /* a CUDA runtime/driver call failed          */
+};
+
+/* Bits reported by cie_read_device_errors(): kernels never trap; a failed
+ * device-side check or a wait that exceeded its time limit sets a bit and
+ * the kernel returns early. */
+enum cie_device_error_bits {
+  CIE_DEVERR_BAD_SLOT = 1u << 0,      /* slot id outside [0, n_slots)             */
+  CIE_DEVERR_BAD_LENGTH = 1u << 1,    /* length exceeds the block-table row       */
+  CIE_DEVERR_BAD_PAGE = 1u << 2,      /* page id outside [0, n_pages)             */
+  CIE_DEVERR_BAD_OFFSET = 1u << 3,    /* in-page offset outside [0, page_size)    */
+  CIE_DEVERR_WAIT_TIMEOUT = 1u << 4,  /* an mbarrier wait ran past its limit      */
+  CIE_DEVERR_BAD_SEQLENS = 1u << 5    /* cu_seqlens not monotone / beyond T       */
+};
+
+/* ---- library-wide ---------------------------------------------------------- */
+
+int cie_version(void);
+const char* cie_status_string(int status);
+const char* cie_last_error_message(void);
+
+/* Copies the device error bits of `device` into *bits and, when `clear` is
+ * non-zero, resets them. Synchronous (it waits for `device`'s prior work). */
+int cie_read_device_errors(int device, unsigned int* bits, int clear);
+
+/* ---- split-KV paged GQA decode ------------------------------------------- */
+
+/* Split count used when cie_decode_attention() is given num_splits <= 0:
+ * enough (sequence, split) CTAs to keep every SM of `device` streaming. */
+int cie_decode_default_splits(int batch, int device);
+
+/* Bytes of fp32 workspace the split path needs (0 when num_splits == 1). */
+size_t cie_decode_workspace_bytes(int batch, int num_q_heads, int head_dim, int num_splits);
+
+/*
+ * One query token per sequence over the paged KV pool.
+ * Replaces attn/core.py:13-66 (decode_gqa_attention) and its kernels
+ * kernels/decode_attention.py:12-179 (load) and :182-272 (merge); this is the
+ * body of the torch op inference::gqa_decode_attention (attn/core.py:119-126).
+ *   sequence b: query q[0, b], slot slot_ids[b], visible rows [0, lens[b])
+ *   (lens includes the token just written by decode_update); lens[b] == 0
+ *   gives a zero output row, as the reference merge does.
+ * num_splits: KV splits per sequence (<= 0: cie_decode_default_splits).
+ * workspace: >= cie_decode_workspace_bytes(...) bytes, 16-byte aligned
+ * (may be NULL when the split count resolves to 1).
+ */
+int cie_decode_attention(const void* q, const void* k, const void* v, const int64_t* lens,
+                         const int64_t* slot_ids, const int64_t* block_table, void* o,
+                         void* workspace, size_t workspace_bytes, int batch, int num_q_heads,
+                         int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
+                         int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
+                         int64_t kv_head_stride, int num_splits, cie_stream_t stream);
+
+/* ---- varlen mixed (chunked prefill + decode) attention --------------------- */
+
+/*
+ * Causal attention for a batch of chunks in one launch.
+ * Replaces attn/core.py:69-111 (mixed_gqa_attention) and its kernel
+ * kernels/prefill_attention.py:10-198; body of inference::gqa_mixed_attention
+ * (attn/core.py:128-137).
+ *   sequence b owns rows [cu_seqlens[b], cu_seqlens[b+1]) of q / o; its row i
+ *   sits at position kv_lens[b] + i and attends to keys [0, kv_lens[b] + i]
+ *   of slot slot_ids[b] (the chunk's own K/V are already in the pool).
+ *   max_seqlen bounds every chunk length (the bucket's token count).
+ *   Rows outside every [cu_seqlens[b], cu_seqlens[b+1]) are not written.
+ */
+int cie_mixed_attention(const void* q, const void* k, const void* v, int64_t max_seqlen,
+                        const int64_t* cu_seqlens, const int64_t* kv_lens,
+                        const int64_t* slot_ids, const int64_t* block_table, void* o,
+                        int batch, int64_t total_tokens, int num_q_heads, int num_kv_heads,
+                        int head_dim, int page_size, int64_t n_pages, int64_t n_slots,
+                        int64_t bt_stride, int64_t kv_page_stride, int64_t kv_head_stride,
+                        cie_stream_t stream);
+
+/* ---- KV-page scatter ------------------------------------------------------- */
+
+/*
+ * Writes each decode token's K and V row into its page.
+ * Replaces KVStorage.decode_update (kv_cache/storage.py:87-122): for
+ * s = slot_ids[i], pos = lens[s] (the slot's length BEFORE this token), the row
+ * lands at page block_table[s * bt_stride + pos / page_size], offset
+ * pos % page_size. k_new / v_new are (1, batch, num_kv_heads, head_dim) views
+ * with token stride *_tok_stride and head stride *_head_stride (elements;
+ * inner stride 1). Bit-exact copy.
+ */
+int cie_kv_decode_update(void* k_cache, void* v_cache, const int64_t* lens,
+                         const int64_t* slot_ids, const int64_t* block_table, const void* k_new,
+                         const void* v_new, int batch, int num_kv_heads, int head_dim,
+                         int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                         int64_t cache_page_stride, int64_t cache_head_stride,
+                         int64_t k_tok_stride, int64_t k_head_stride, int64_t v_tok_stride,
+                         int64_t v_head_stride, cie_stream_t stream);
+
+/*
+ * Writes token t's K and V row to page pages[t], offset offsets[t].
+ * Replaces KVStorage.mixed_update (kv_cache/storage.py:62-85). Bit-exact copy.
+ */
+int cie_kv_mixed_update(void* k_cache, void* v_cache, const int64_t* pages,
+                        const int64_t* offsets, const void* k_new, const void* v_new,
+                        int64_t num_tokens, int num_kv_heads, int head_dim, int page_size,
+                        int64_t n_pages, int64_t cache_page_stride, int64_t cache_head_stride,
+                        int64_t k_tok_stride, int64_t k_head_stride, int64_t v_tok_stride,
+                        int64_t v_head_stride, cie_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CIE_ATTENTION_H_ */

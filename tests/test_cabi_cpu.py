@@ -1,0 +1,88 @@
+"""The C-ABI library loads without a GPU, exports every symbol the header
+declares, and rejects bad arguments on the host before launching anything."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from custom_inference_engine_b200 import native
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "cie_attention.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(cie_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_header_declares_the_expected_entry_points():
+    names = declared_functions()
+    for must in ("cie_decode_attention", "cie_mixed_attention", "cie_kv_decode_update",
+                 "cie_kv_mixed_update", "cie_decode_workspace_bytes"):
+        assert must in names
+
+
+def test_every_declared_symbol_is_exported():
+    handle = ctypes.CDLL(str(native.LIB_PATH))
+    for name in declared_functions():
+        assert hasattr(handle, name), name
+    assert set(declared_functions()) == set(native.SIGNATURES)
+
+
+def test_host_only_queries():
+    lib = native.lib()
+    assert lib.cie_version() >= 1
+    assert lib.cie_status_string(-2) == b"unsupported shape"
+    assert lib.cie_decode_workspace_bytes(256, 14, 64, 1) == 0
+    assert lib.cie_decode_workspace_bytes(8, 14, 64, 4) == 8 * 4 * 14 * 66 * 4
+    assert lib.cie_decode_default_splits(0, -1) == 1
+    assert lib.cie_decode_default_splits(256, -1) == 1
+    assert lib.cie_decode_default_splits(8, -1) == 37
+
+
+def _decode(**kw):
+    args = dict(q=1 << 20, k=1 << 21, v=1 << 22, lens=1 << 23, slot_ids=1 << 24, bt=1 << 25,
+                o=1 << 26, ws=None, ws_bytes=0, batch=4, hq=14, hkv=2, d=64, page=16,
+                n_pages=100, n_slots=5, bt_stride=100, pstride=2048, hstride=1024, splits=1,
+                stream=None)
+    args.update(kw)
+    return native.lib().cie_decode_attention(*args.values())
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(q=None), -1),
+    (dict(batch=-1), -1),
+    (dict(d=128), -2),
+    (dict(page=32), -2),
+    (dict(hq=16), -2),
+    (dict(hkv=3, hq=21), -2),
+    (dict(n_pages=1 << 31), -3),
+    (dict(pstride=2000), -1),
+    (dict(pstride=2052, hstride=1026), -4),
+    (dict(k=(1 << 21) + 2), -4),
+    (dict(splits=4), -5),
+])
+def test_decode_argument_checks(kw, status):
+    assert _decode(**kw) == status
+    assert native.lib().cie_last_error_message()
+
+
+def test_decode_empty_batch_is_a_no_op():
+    assert _decode(batch=0, q=None) == 0
+
+
+def test_mixed_and_update_argument_checks():
+    lib = native.lib()
+    p = 1 << 20
+    assert lib.cie_mixed_attention(p, p, p, 16, p, p, p, p, p, 2, 16, 14, 2, 128, 16, 10, 3, 10,
+                                   4096, 2048, None) == -2
+    assert lib.cie_mixed_attention(None, p, p, 16, p, p, p, p, p, 2, 16, 14, 2, 64, 16, 10, 3,
+                                   10, 2048, 1024, None) == -1
+    assert lib.cie_mixed_attention(p, p, p, 0, p, p, p, p, p, 2, 16, 14, 2, 64, 16, 10, 3, 10,
+                                   2048, 1024, None) == 0
+    assert lib.cie_kv_mixed_update(None, p, p, p, p, p, 4, 2, 64, 16, 10, 2048, 1024, 1152, 64,
+                                   1152, 64, None) == -1
+    assert lib.cie_kv_decode_update(p, p, p, p, p, p, p, 4, 2, 64, 16, 10, 3, 10, 100, 1024,
+                                    1152, 64, 1152, 64, None) == -1
