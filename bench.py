@@ -51,7 +51,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=256)
@@ -61,6 +61,10 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bound on the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-mixed", action="store_true", help="skip the mixed-attention lines")
+    ap.add_argument("--sweep", action="store_true",
+                    help="print one JSON line per decode sweep point (configs 2 and 5) "
+                         "instead of the benchmark line")
     return ap.parse_args(argv)
 
 
@@ -149,21 +153,36 @@ class ClockSampler:
     def __init__(self, device_index: int):
         self.proc = None
         self.lines = []
+        self.index = self._smi_index(device_index)
+
+    @staticmethod
+    def _smi_index(device_index: int):
+        """nvidia-smi index of torch device ``device_index`` (matched by PCI bus id)."""
         try:
-            bus = torch.cuda.get_device_properties(device_index).pci_bus_id
+            props = torch.cuda.get_device_properties(device_index)
+            want = "%02x:%02x.0" % (int(props.pci_bus_id), int(props.pci_device_id))
+            out = subprocess.run(["nvidia-smi", "--query-gpu=index,pci.bus_id",
+                                  "--format=csv,noheader"], capture_output=True, text=True,
+                                 timeout=30).stdout
         except Exception:
-            bus = None
-        self.bus = bus
+            return None
+        for ln in out.splitlines():
+            idx, _, pci = (x.strip() for x in ln.partition(","))
+            if pci.lower().endswith(want):
+                return idx
+        if not os.environ.get("CUDA_VISIBLE_DEVICES"):
+            return str(device_index)
+        return None
 
     def __enter__(self):
-        if self.bus is None:
+        if self.index is None:
             return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.bus)],
+                 "-lms", "100", "-i", str(self.index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            time.sleep(0.3)
+            time.sleep(0.5)
         except Exception:
             self.proc = None
         return self
@@ -211,7 +230,7 @@ def decode_bytes(batch: int, kv_len: int) -> int:
 # CPU legs (oracle port)
 # ---------------------------------------------------------------------------
 
-def cpu_oracle_rate(kv_len: int, seconds: float, max_seqs: int = 64):
+def cpu_oracle_rate(kv_len: int, seconds: float, max_seqs: int = 1 << 20):
     """Times the fp32 CPU oracle on sequences of ``kv_len`` until ``seconds``
     elapse; returns (GB/s, threads, sample description)."""
     import oracle
@@ -283,6 +302,102 @@ def workload_config(args, world):
 # ---------------------------------------------------------------------------
 # GPU leg
 # ---------------------------------------------------------------------------
+
+L2_FLUSH_BYTES = 256 << 20   # twice the 126 MB L2
+
+
+def time_launches(fn, iters: int, flush: bool, dev):
+    """Per-call device time (ms) of ``fn`` with CUDA events on the current
+    stream; with ``flush`` a buffer larger than L2 is rewritten before each
+    call, outside the timed pair."""
+    stream = torch.cuda.current_stream()
+    scratch = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
+    pairs = []
+    for _ in range(iters):
+        if flush:
+            scratch.fill_(1.0)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        pairs.append((a, b))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in pairs]
+
+
+def bf16_peak_tflops(sustained: bool = False):
+    p = REPO / "MEASURED_PEAKS.json"
+    key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())[key]), "measured " + key
+        except Exception:
+            pass
+    return (1400.0 if sustained else 1590.0), "fallback"
+
+
+def mixed_lines(dev, iters: int = 30):
+    """Mixed attention: the 512-token-chunk variant (tensor roofline) and
+    config 3 (32 sequences, chunk 1 w.p. 0.5 else U[16,512], budget 2048)."""
+    from custom_inference_engine_b200 import workloads as W
+    from custom_inference_engine_b200.attn import core
+    out = {}
+    g = torch.Generator().manual_seed(1)
+    kv512 = torch.randint(0, 8193, (4,), generator=g).tolist()
+    chunk3, kv3 = W.config3_shape(seed=0)
+    cases = {
+        "mixed_512_chunks": W.make_mixed_case([512] * 4, kv512, seed=1, device=dev,
+                                              generate_on_device=True),
+        "mixed_config3": W.make_mixed_case(chunk3, kv3, seed=0, device=dev, max_seqlen=2048,
+                                           generate_on_device=True),
+    }
+    peak, src = bf16_peak_tflops()
+    for name, c in cases.items():
+        def fn(c=c):
+            core.gqa_mixed_attention_op(c.q, c.k, c.v, max_seqlen=c.max_seqlen,
+                                        cu_seqlens=c.cu_seqlens, kv_lens=c.kv_lens,
+                                        slot_ids=c.slot_ids, block_table=c.block_table)
+        for _ in range(3):
+            fn()
+        ms = statistics.median(time_launches(fn, iters, flush=True, dev=dev))
+        flops = c.causal_flops()
+        tflops = flops / (ms / 1e3) / 1e12
+        out[name] = {"ms_per_call": ms, "tflops": tflops, "causal_flops": flops,
+                     "tensor_frac": tflops / peak, "peak_tflops": peak, "peak_source": src,
+                     "hbm_gbs": c.algorithmic_bytes() / (ms / 1e3) / 1e9,
+                     "chunks": c.chunk_lens(), "kv_lens": c.kv_lens.tolist(),
+                     "l2": "flushed before each call"}
+    return out
+
+
+def run_sweep(args, dev):
+    """Config 2 (B x kv_len) and config 5 (64 x 32768 split sweep, 8 per GPU) points."""
+    from custom_inference_engine_b200 import cabi
+    from custom_inference_engine_b200 import workloads as W
+    from custom_inference_engine_b200.attn import core
+    peak, _ = measured_peak_gbs()
+    points = [(b, l, 0) for l in (512, 4096, 16384) for b in (1, 2, 4, 8, 16, 32, 64, 128, 256)]
+    points += [(8, 32768, s) for s in (4, 8, 16, 32, 64)]
+    for B, L, S in points:
+        c = W.make_decode_case([L] * B, seed=5, device=dev, generate_on_device=True)
+        splits = S if S > 0 else cabi.decode_default_splits(B, dev.index)
+
+        def fn():
+            core.decode_gqa_attention(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table,
+                                      num_programs=splits)
+        for _ in range(3):
+            fn()
+        kv_bytes = B * L * 512
+        ms = statistics.median(time_launches(fn, 50, flush=kv_bytes < (256 << 20), dev=dev))
+        nbytes = decode_bytes(B, L)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        print(json.dumps({"sweep": "config5" if S else "config2", "batch": B, "kv_len": L,
+                          "num_splits": splits, "us_per_call": ms * 1e3, "gbs": gbs,
+                          "frac_of_measured_hbm": gbs / peak}), flush=True)
+        del c
+        torch.cuda.empty_cache()
+
 
 def run_ours(args, rank, world, local):
     from custom_inference_engine_b200 import cabi, native
@@ -383,6 +498,8 @@ def run_ours(args, rank, world, local):
             "clocks": clocks.summary(),
             "device_error_bits": errs,
         }
+        if not args.no_mixed:
+            result["mixed"] = mixed_lines(dev)
         if not args.no_cpu_baseline and world == 1:
             gbs, cores, sample = cpu_oracle_rate(L, args.cpu_seconds)
             result["cpu_baseline"] = {"value": gbs, "unit": UNIT, "cores": cores, "kind": "port",
@@ -394,7 +511,11 @@ def main(argv=None):
     args = parse_args(argv)
     rank, world, local = dist_setup(args)
     try:
-        if args.impl == "reference":
+        if args.sweep:
+            if rank == 0:
+                run_sweep(args, torch.device("cuda", torch.cuda.current_device()))
+            res = None
+        elif args.impl == "reference":
             res = run_reference(args, rank, world)
         else:
             res = run_ours(args, rank, world, local)
