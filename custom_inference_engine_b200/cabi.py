@@ -47,6 +47,20 @@ def decode_attention(q, k, v, lens, slot_ids, block_table, out=None, num_splits:
     return out
 
 
+def decode_attention_noalloc(q, k, v, lens, slot_ids, block_table, out=None,
+                             num_splits: int = 0, stream=None) -> torch.Tensor:
+    """cie_decode_attention_noalloc: same result, split scratch inside the library."""
+    if out is None:
+        out = torch.empty_like(q)
+    st = native.lib().cie_decode_attention_noalloc(
+        _p(q), _p(k), _p(v), _p(lens), _p(slot_ids), _p(block_table), _p(out),
+        slot_ids.shape[0], q.shape[2], k.shape[1], q.shape[3], k.shape[2], k.shape[0],
+        block_table.shape[0], block_table.stride(0), k.stride(0), k.stride(1), num_splits,
+        native.stream_ptr(stream))
+    native.check(st, "cie_decode_attention_noalloc")
+    return out
+
+
 def mixed_attention(q, k, v, max_seqlen: int, cu_seqlens, kv_lens, slot_ids, block_table,
                     out=None, stream=None) -> torch.Tensor:
     """cie_mixed_attention; rows outside every sequence are left as they were in ``out``."""

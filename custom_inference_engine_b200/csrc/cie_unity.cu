@@ -3,5 +3,6 @@
 // device code.
 #include "cie_api.cu"
 #include "decode_attention.cu"
+#include "decode_noalloc.cu"
 #include "kv_update.cu"
 #include "mixed_attention.cu"

@@ -40,6 +40,9 @@ SIGNATURES = {
     "cie_decode_attention": (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
                                      c_size, c_int, c_int, c_int, c_int, c_int, c_i64, c_i64,
                                      c_i64, c_i64, c_i64, c_int, c_ptr]),
+    "cie_decode_attention_noalloc": (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
+                                             c_int, c_int, c_int, c_int, c_int, c_i64, c_i64,
+                                             c_i64, c_i64, c_i64, c_int, c_ptr]),
     "cie_mixed_attention": (c_int, [c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
                                     c_ptr, c_int, c_i64, c_int, c_int, c_int, c_int, c_i64,
                                     c_i64, c_i64, c_i64, c_i64, c_ptr]),

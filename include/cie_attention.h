@@ -4,9 +4,11 @@
  *
  * Every entry point takes plain device pointers, sizes and strides (in
  * elements), launches asynchronously on `stream`, performs no host<->device
- * synchronisation and allocates nothing, so each call can be captured in a
- * CUDA graph. Return value: CIE_OK or a negative cie_status; on error nothing
- * was launched and cie_last_error_message() (thread-local) says why.
+ * synchronisation and allocates nothing. cie_decode_attention,
+ * cie_mixed_attention, cie_kv_decode_update and cie_kv_mixed_update can be
+ * captured in a CUDA graph. Return value: CIE_OK or a negative cie_status; on
+ * error nothing was launched and cie_last_error_message() (thread-local) says
+ * why.
  *
  * Layouts are the reference engine's (eteboun/custom_inference_engine):
  *   q / o        (1, T, num_q_heads, head_dim)  fp16, contiguous
@@ -16,7 +18,7 @@
  *                block_table[s * bt_stride + j]   (kv_cache/storage.py:54-56)
  *   lens, kv_lens, slot_ids, pages, offsets: int64; cu_seqlens: int64 (B+1)
  * Supported shapes: head_dim 64, page_size 16, num_q_heads / num_kv_heads = 7
- * (Qwen2.5-0.5B: 14 / 2), num_kv_heads <= 8.
+ * (Qwen2.5-0.5B: 14 / 2); decode takes num_kv_heads 1, 2 or 4.
  */
 #ifndef CIE_ATTENTION_H_
 #define CIE_ATTENTION_H_
@@ -90,6 +92,34 @@ int cie_decode_attention(const void* q, const void* k, const void* v, const int6
                          int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
                          int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
                          int64_t kv_head_stride, int num_splits, cie_stream_t stream);
+
+/*
+ * Same computation and arguments as cie_decode_attention, minus the workspace:
+ * the split partials go to a scratch array inside this library, so the call
+ * allocates nothing and the caller passes only inputs and outputs.
+ * No counterpart in the reference: it exists for callers that cannot allocate
+ * device memory -- a host that only holds device pointers handed over an FFI
+ * and has no device allocator, or a process that reserved all of HBM for
+ * weights and the KV pool, where another cudaMalloc would fail or, because
+ * cudaMalloc / cudaFree synchronise the device, stall the decode loop.
+ * Limit: cie_decode_workspace_bytes(batch, num_q_heads, head_dim, splits) must
+ * not exceed CIE_DECODE_NOALLOC_SCRATCH_BYTES (4 MiB, i.e. batch x splits <= 1134
+ * for 14 heads of 64); larger requests return CIE_ERR_WORKSPACE.
+ * Every GPU that loads the library holds the 4 MiB until the process exits.
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture. All calls
+ * on a device share the array and it keeps the last call's contents (nothing
+ * in it needs to start at zero); calls that overlap on the GPU race on it.
+ */
+#define CIE_DECODE_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+int cie_decode_attention_noalloc(const void* q, const void* k, const void* v,
+                                 const int64_t* lens, const int64_t* slot_ids,
+                                 const int64_t* block_table, void* o, int batch,
+                                 int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                 int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                                 int64_t kv_page_stride, int64_t kv_head_stride, int num_splits,
+                                 cie_stream_t stream);
 
 /* ---- varlen mixed (chunked prefill + decode) attention --------------------- */
 
