@@ -63,6 +63,27 @@ struct Params {
   int64_t bt_stride;
 };
 
+// Fewest pages a split is given: below this the fixed cost of a CTA (start-up,
+// first TMA round trip, its partial) outweighs the bytes it streams.
+constexpr int kMinPagesPerSplit = 4;
+
+// Pages of sequence b that the kernels visit; 0 for an invalid slot. A length
+// beyond the block-table row is clamped to it.
+__device__ __forceinline__ int seq_pages(const int64_t* lens, const int64_t* slot_ids, int b,
+                                         int64_t n_slots, int64_t bt_stride) {
+  const int64_t slot = slot_ids[b];
+  if (slot < 0 || slot >= n_slots) return 0;
+  int64_t L = lens[b];
+  if (L < 0) L = 0;
+  const int64_t np = (L + kPage - 1) / kPage;
+  return static_cast<int>(np > bt_stride ? bt_stride : np);
+}
+
+// Contiguous pages per split (the same partition in the split and merge kernels).
+__device__ __forceinline__ int split_pages(int n_seq_pages, int S) {
+  return max((n_seq_pages + S - 1) / S, kMinPagesPerSplit);
+}
+
 __device__ __forceinline__ float shfl_max_group(float x) {
   x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
   x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
@@ -113,7 +134,7 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
   }
   if (bad) L = 0;
   const int n_seq_pages = static_cast<int>((L + kPage - 1) / kPage);
-  const int pps = (n_seq_pages + S - 1) / S;
+  const int pps = split_pages(n_seq_pages, S);
   const int page_begin = split * pps;
   const int n = max(0, min(page_begin + pps, n_seq_pages) - page_begin);
   const int Li = static_cast<int>(L);
@@ -124,6 +145,9 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
       mbar_init(empty0 + 8u * s, HKV);
     }
     fence_mbar_init();
+    // let the merge kernel (launched with programmatic stream serialization)
+    // get scheduled while this grid streams; it waits for our completion
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   }
   __syncthreads();
 
@@ -134,18 +158,22 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
       tma_prefetch_desc(&tm_v);
     }
     const int64_t* bt_row = p.block_table + slot * p.bt_stride + page_begin;
+    auto page_id = [&](int j) -> int {  // block-table entry j of this split, checked
+      if (j >= n) return 0;
+      int64_t pid = bt_row[j];
+      if (pid < 0 || pid >= p.n_pages) {
+        raise_error(CIE_DEVERR_BAD_PAGE);
+        pid = 0;
+      }
+      return static_cast<int>(pid);
+    };
     bool abort = false;
     int issued = 0;
+    int next_page = page_id(lane);
     for (int base = 0; base < n && !abort; base += 32) {
-      int page = 0;
-      if (base + lane < n) {
-        int64_t pid = bt_row[base + lane];
-        if (pid < 0 || pid >= p.n_pages) {
-          raise_error(CIE_DEVERR_BAD_PAGE);
-          pid = 0;
-        }
-        page = static_cast<int>(pid);
-      }
+      const int page = next_page;
+      // fetch the next 32 entries now; they are needed only after this batch
+      next_page = page_id(base + 32 + lane);
       const int cnt = min(32, n - base);
       for (int t = 0; t < cnt; ++t) {
         const int pg = __shfl_sync(0xffffffffu, page, t);
@@ -211,7 +239,9 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
   for (int i = par; i < n; i += 2) {
     const int s = i % C::kStages;
     const uint32_t use = static_cast<uint32_t>(i / C::kStages);
-    if (!mbar_wait(full0 + 8u * s, use & 1u, CIE_DEVERR_WAIT_TIMEOUT)) break;
+    // ldmatrix / mma / movmatrix below are warp-collective: leave together
+    if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8u * s, use & 1u, CIE_DEVERR_WAIT_TIMEOUT)))
+      break;
     // Head h's 16 rows start at a multiple of 1 KiB inside the stage, so the
     // 128B-swizzle phase of row r is r mod 8.
     const uint32_t kt = ring_u32 + s * C::kStageBytes + h * kHeadTileBytes;
@@ -353,7 +383,7 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
     const uint4* src = reinterpret_cast<const uint4*>(stage);
     uint4* dst = reinterpret_cast<uint4*>(p.o + (static_cast<int64_t>(b) * H_Q + h * kGroup) * kD);
     for (int e = lane; e < kGroup * kD / 8; e += 32) dst[e] = src[e];
-  } else {
+  } else if (n > 0) {  // the merge reads only splits that saw pages
     const int64_t base = (static_cast<int64_t>(b) * S + split) * H_Q;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -373,38 +403,69 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
   }
 }
 
-// Combines the split partials of one sequence: O = sum_s w_s acc_s / sum_s w_s l_s,
-// w_s = exp(m_s - max m); splits that saw no key (m = -inf) are skipped and a
-// sequence with no key at all gets a zero row (reference merge,
-// kernels/decode_attention.py:243-264).
+// Combines the split partials of one (query head, sequence):
+// O = sum_s w_s acc_s / sum_s w_s l_s, w_s = exp(m_s - max m), over the splits
+// that saw pages; a sequence with no key at all gets a zero row (reference
+// merge, kernels/decode_attention.py:243-264). 8 warps each fold every 8th
+// split (lane = two output columns), then warp 0 folds the 8 warp results.
+// Launched with programmatic stream serialization: griddepcontrol.wait holds
+// it until the split kernel has finished and its writes are visible.
 __global__ void __launch_bounds__(256)
     decode_merge_kernel(const float* __restrict__ ws_acc, const float* __restrict__ ws_ml,
-                        __half* __restrict__ o, int num_splits, int num_q_heads) {
-  const int b = blockIdx.x;
+                        __half* __restrict__ o, const int64_t* __restrict__ lens,
+                        const int64_t* __restrict__ slot_ids, int64_t n_slots,
+                        int64_t bt_stride, int num_splits, int num_q_heads) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float s_m[8], s_l[8];
+  __shared__ float2 s_acc[8][32];
+  const int hq = blockIdx.x;
+  const int b = blockIdx.y;
   const int S = num_splits;
-  for (int idx = threadIdx.x; idx < num_q_heads * (kD / 2); idx += blockDim.x) {
-    const int hq = idx / (kD / 2);
-    const int d = (idx % (kD / 2)) * 2;
-    const int64_t base = static_cast<int64_t>(b) * S * num_q_heads;
-    float M = -CUDART_INF_F;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, ws_ml[((base + s * num_q_heads) + hq) * 2]);
-    float den = 0.f, n0 = 0.f, n1 = 0.f;
-    if (M != -CUDART_INF_F) {
-      for (int s = 0; s < S; ++s) {
-        const int64_t r = base + s * num_q_heads + hq;
-        const float m = ws_ml[r * 2];
-        if (m == -CUDART_INF_F) continue;
-        const float w = ex2((m - M) * kLog2e);
-        den += w * ws_ml[r * 2 + 1];
-        const float2 a = *reinterpret_cast<const float2*>(ws_acc + r * kD + d);
-        n0 += w * a.x;
-        n1 += w * a.y;
-      }
-    }
-    const float inv = den > 0.f ? 1.f / den : 0.f;
-    *reinterpret_cast<__half2*>(o + (static_cast<int64_t>(b) * num_q_heads + hq) * kD + d) =
-        __floats2half2_rn(n0 * inv, n1 * inv);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int np = seq_pages(lens, slot_ids, b, n_slots, bt_stride);
+  const int pps = split_pages(np, S);
+  const int active = np == 0 ? 0 : (np + pps - 1) / pps;
+
+  float M = -CUDART_INF_F, l = 0.f;
+  float2 acc = make_float2(0.f, 0.f);
+  for (int s = warp; s < active; s += 8) {
+    const int64_t r = (static_cast<int64_t>(b) * S + s) * num_q_heads + hq;
+    const float m = ws_ml[r * 2];   // finite: every active split saw a key
+    const float ls = ws_ml[r * 2 + 1];
+    const float2 a = *reinterpret_cast<const float2*>(ws_acc + r * kD + 2 * lane);
+    const float Mn = fmaxf(M, m);
+    const float wo = ex2((M - Mn) * kLog2e);
+    const float wn = ex2((m - Mn) * kLog2e);
+    l = l * wo + ls * wn;
+    acc.x = acc.x * wo + a.x * wn;
+    acc.y = acc.y * wo + a.y * wn;
+    M = Mn;
   }
+  if (lane == 0) {
+    s_m[warp] = M;
+    s_l[warp] = l;
+  }
+  s_acc[warp][lane] = acc;
+  __syncthreads();
+  if (warp != 0) return;
+  float Mt = -CUDART_INF_F;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) Mt = fmaxf(Mt, s_m[w]);
+  float den = 0.f;
+  float2 num = make_float2(0.f, 0.f);
+  if (Mt != -CUDART_INF_F) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float wt = s_m[w] == -CUDART_INF_F ? 0.f : ex2((s_m[w] - Mt) * kLog2e);
+      den += wt * s_l[w];
+      num.x += wt * s_acc[w][lane].x;
+      num.y += wt * s_acc[w][lane].y;
+    }
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  *reinterpret_cast<__half2*>(o + (static_cast<int64_t>(b) * num_q_heads + hq) * kD + 2 * lane) =
+      __floats2half2_rn(num.x * inv, num.y * inv);
 }
 
 template <int HKV>
@@ -447,8 +508,19 @@ int launch(const void* q, const void* k, const void* v, const int64_t* lens,
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   if (S > 1) {
-    decode_merge_kernel<<<batch, 256, 0, stream>>>(p.ws_acc, p.ws_ml, p.o, S, H_Q);
-    e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(H_Q, batch);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, decode_merge_kernel, static_cast<const float*>(p.ws_acc),
+                           static_cast<const float*>(p.ws_ml), p.o, lens, slot_ids, n_slots,
+                           bt_stride, S, H_Q);
     if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
   }
   return CIE_OK;

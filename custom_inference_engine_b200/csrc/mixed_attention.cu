@@ -4,28 +4,48 @@
 // Replaces mixed_gqa_attention_kernel (kernels/prefill_attention.py:10-198)
 // behind the host contract of attn/core.py:69-111.
 //
-// One CTA owns one query tile of one (sequence, kv head): 18 consecutive
+// Work unit: one CTA = TWO consecutive query tiles (A, B) of one
+// (sequence, kv head) x one contiguous range of 128-key blocks. A tile is 18
 // tokens x the 7 query heads that share the kv head = 126 rows of the
 // tcgen05 M = 128 tile (the reference pads 7 heads to 8 and uses 16 tokens,
-// 112 useful rows of 128). The tile is a single TMA box over q viewed as
-// (token, kv head, head-in-group, dim), so row r = token * 7 + head.
+// 112 useful rows of 128); it is one TMA box over q viewed as
+// (token, kv head, head-in-group, dim), row r = token * 7 + head. Both tiles
+// consume the same K/V blocks, loaded once. When a tile pair's keys are split
+// over several CTAs, each writes an fp32 partial (m, l, unnormalised O) per
+// row and a merge kernel combines them; a pair that is not split writes O.
 //
-// Warp roles (192 threads):
-//   warp 0      TMA producer: the Q tile once, then per 128-key block the
-//               8 K pages and 8 V pages of this kv head (2 KiB boxes through
-//               the block table) into a 3-stage ring;
-//   warp 1      TMEM owner and single-thread MMA issuer:
-//               S_j = Q K_j^T (M128 N128 K16 x4) into one of two S buffers,
-//               then PV_{j-1} = P_{j-1} V_{j-1} (M128 N64 K16 x8) into one of
-//               two PV buffers, so block j's QK^T overlaps block j-1's softmax;
-//   warps 2-5   softmax: thread = TMEM lane = tile row. Reads S_j, applies
-//               scale, causal limit and online max, writes fp16 P_j to shared
-//               memory in the 128B-swizzled K-major layout the MMA reads, then
-//               folds PV_{j-1} into fp32 registers: O = O * alpha + PV, the
-//               same update as the reference (acc * alpha + dot(P, V)).
+// Warp roles (576 threads):
+//   warp 0       TMA producer: both Q tiles, then per key block the 8 K and
+//                8 V pages of this kv head (2 KiB boxes through the block
+//                table) into a 3-stage ring.
+//   warp 1       TMEM owner and single-thread, event-driven MMA issuer:
+//                S_x(j+1) = Q_x K_{j+1}^T as soon as K_{j+1} is in and tile x's
+//                softmax has read S_x(j); PV for each (tile, key half) as soon
+//                as that half of P_x(j) is published. The next QK^T therefore
+//                runs while the softmax works on this block, and no tile or
+//                half waits behind another.
+//   warps 2-9    softmax of tile A, warps 10-17 of tile B: two warps per TMEM
+//                lane quadrant, one for key columns 0-63 of every block, one
+//                for 64-127. Each half keeps its OWN online softmax (reference
+//                max m, sum l) and its own O accumulator in TMEM
+//                (O_h += P[:, half] V[half, :], issued per half), so the two
+//                halves never synchronise inside the key loop; they are
+//                combined once at the end like two split-KV partials. The
+//                exponentials of a block are computed into registers before
+//                waiting for the previous block's PV of the half. A half
+//                moves its reference max only when the block maximum exceeds
+//                it by more than 2^8 (and then rescales O_h and l): P stays
+//                <= 256, exact in fp16, and O / l is the reference's softmax
+//                (acc * alpha + dot(P, V), kernels/prefill_attention.py:
+//                157-184) up to rounding. Warps whose 32 rows are all padding
+//                (short chunks, decode rows) do nothing; barrier arrival
+//                counts only cover the working warps.
+// CTAs run most-expensive first: blockIdx.y walks the tile pairs from the
+// last (most keys) to the first.
 // All waits are bounded; on a timeout the kernel records
 // CIE_DEVERR_WAIT_TIMEOUT, drains its own copies and MMAs, frees TMEM and
-// returns.
+// returns. tcgen05.ld / st / wait are warp-collective, so every decision that
+// guards one is warp-uniform.
 #include <math_constants.h>
 
 #include "cie_common.cuh"
@@ -38,33 +58,44 @@ constexpr int kD = 64;
 constexpr int kPage = 16;
 constexpr int kGroup = 7;
 constexpr int kTileTokens = 18;
+constexpr int kPairTokens = 2 * kTileTokens;
 constexpr int kRows = kTileTokens * kGroup;  // 126 useful rows of M = 128
 constexpr int kM = 128;
 constexpr int kBlockKeys = 128;
+constexpr int kHalfKeys = kBlockKeys / 2;
 constexpr int kPagesPerBlock = kBlockKeys / kPage;  // 8
 constexpr int kStages = 3;
-constexpr int kThreads = 192;
+constexpr int kMinBlocksPerSplit = 2;
+constexpr int kMaxSplits = 16;
+constexpr int kTileThreads = 256;                   // softmax threads per tile
+constexpr int kThreads = 64 + 2 * kTileThreads;
+constexpr float kRescaleLog2 = 8.f;                 // move the max when it grows by > 2^8
 
-constexpr int kQBytes = kM * kD * 2;             // 16 KiB
-constexpr int kQLoadBytes = kRows * kD * 2;      // 16128 bytes delivered by the box
+constexpr int kQBytes = kM * kD * 2;               // 16 KiB
+constexpr int kQLoadBytes = kRows * kD * 2;        // 16128 bytes delivered by one box
 constexpr int kKVTileBytes = kBlockKeys * kD * 2;  // 16 KiB per K or V block
 constexpr int kStageBytes = 2 * kKVTileBytes;
-constexpr int kPBytes = kM * kBlockKeys * 2;     // 32 KiB
-constexpr int kPageBoxBytes = kPage * kD * 2;    // 2 KiB
+constexpr int kPBytes = kM * kBlockKeys * 2;       // 32 KiB
+constexpr int kPageBoxBytes = kPage * kD * 2;      // 2 KiB
 
-constexpr int kOffQ = 0;
-constexpr int kOffKV = kOffQ + kQBytes;
-constexpr int kOffP = kOffKV + kStages * kStageBytes;
-constexpr int kOffBar = kOffP + 2 * kPBytes;
-// barriers: kv_full[3], kv_empty[3], q_full, s_full[2], s_free[2], p_full[2],
-// pv_full[2], pv_free[2], mma_done; then the TMEM base address
-constexpr int kNumBars = 2 * kStages + 1 + 2 * 5 + 1;
+constexpr int kOffQ = 0;                                   // Q_A, Q_B
+constexpr int kOffKV = kOffQ + 2 * kQBytes;
+constexpr int kOffP = kOffKV + kStages * kStageBytes;      // P_A, P_B
+constexpr int kOffRed = kOffP + 2 * kPBytes;               // [tile][half][row] x (m, l)
+constexpr int kRedBytes = 2 * 2 * kM * 8;
+constexpr int kOffBar = kOffRed + kRedBytes;
+// barriers: kv_full[3], kv_empty[3], q_full, mma_done, then per tile:
+// s_full, s_free, p_full[2 halves], pv_done[2 halves], red_ready
+constexpr int kTileBars = 7;
+constexpr int kNumBars = 2 * kStages + 2 + 2 * kTileBars;
 constexpr int kOffTmemPtr = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = 1024 + kOffTmemPtr + 16;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;     // two 128-column S buffers
-constexpr uint32_t kColPV = 256;  // two 64-column PV buffers
+// per tile x: S at 256x (128 columns), O of key half h at 256x + 128 + 64h
+constexpr uint32_t kColS = 0;
+constexpr uint32_t kColO = 128;
 
 constexpr uint32_t kIdescS = idesc_f16_f32(kM, kBlockKeys, false);
 constexpr uint32_t kIdescPV = idesc_f16_f32(kM, kD, true);
@@ -75,26 +106,106 @@ struct Params {
   const int64_t* slot_ids;
   const int64_t* block_table;
   __half* o;
+  float* part;  // [split][token][q head] x (acc[64], m, l), only when splits > 1
   int64_t total_tokens;
   int64_t max_seqlen;
   int64_t n_pages;
   int64_t n_slots;
   int64_t bt_stride;
   int num_q_heads;
+  int num_kv_heads;
+  int num_splits;
 };
+
+constexpr int kPartFloats = kD + 2;
 
 struct Bars {
   uint32_t base;
   __device__ uint32_t kv_full(int s) const { return base + 8u * s; }
   __device__ uint32_t kv_empty(int s) const { return base + 8u * (kStages + s); }
   __device__ uint32_t q_full() const { return base + 8u * (2 * kStages); }
-  __device__ uint32_t s_full(int b) const { return base + 8u * (2 * kStages + 1 + b); }
-  __device__ uint32_t s_free(int b) const { return base + 8u * (2 * kStages + 3 + b); }
-  __device__ uint32_t p_full(int b) const { return base + 8u * (2 * kStages + 5 + b); }
-  __device__ uint32_t pv_full(int b) const { return base + 8u * (2 * kStages + 7 + b); }
-  __device__ uint32_t pv_free(int b) const { return base + 8u * (2 * kStages + 9 + b); }
-  __device__ uint32_t mma_done() const { return base + 8u * (2 * kStages + 11); }
+  __device__ uint32_t mma_done() const { return base + 8u * (2 * kStages + 1); }
+  __device__ uint32_t tile(int x, int i) const {
+    return base + 8u * (2 * kStages + 2 + x * kTileBars + i);
+  }
+  __device__ uint32_t s_full(int x) const { return tile(x, 0); }
+  __device__ uint32_t s_free(int x) const { return tile(x, 1); }
+  __device__ uint32_t p_full(int x, int h) const { return tile(x, 2 + h); }
+  __device__ uint32_t pv_done(int x, int h) const { return tile(x, 4 + h); }
+  __device__ uint32_t red_ready(int x) const { return tile(x, 6); }
 };
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns (load and store).
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// ---- the work decomposition, shared with the merge kernel -------------------
+
+struct PairInfo {
+  int L;            // chunk length of the sequence
+  int tok0;         // first token of the pair inside the chunk
+  int pair_tokens;  // tokens of the pair (1..36)
+  int kv_len;
+  int n_blocks;     // key blocks the pair's last row needs
+  int bps;          // blocks per split
+  int n_active;     // splits that own at least one block
+  bool valid;
+};
+
+__device__ __forceinline__ PairInfo pair_info(const Params& p, int b, int pair, bool report) {
+  PairInfo pi{};
+  pi.valid = false;
+  const int64_t start = p.cu_seqlens[b];
+  const int64_t end = p.cu_seqlens[b + 1];
+  if (start < 0 || end < start || end > p.total_tokens) {
+    if (report) raise_error(CIE_DEVERR_BAD_SEQLENS);
+    return pi;
+  }
+  const int64_t L64 = end - start;
+  if (report && pair == 0 && L64 > p.max_seqlen) raise_error(CIE_DEVERR_BAD_SEQLENS);
+  const int tok0 = pair * kPairTokens;
+  if (tok0 >= L64) return pi;
+  const int64_t slot = p.slot_ids[b];
+  if (slot < 0 || slot >= p.n_slots) {
+    if (report) raise_error(CIE_DEVERR_BAD_SLOT);
+    return pi;
+  }
+  int64_t kv_len = p.kv_lens[b];
+  if (kv_len < 0) kv_len = 0;
+  if ((kv_len + L64 + kPage - 1) / kPage > p.bt_stride) {
+    if (report) raise_error(CIE_DEVERR_BAD_LENGTH);
+    return pi;
+  }
+  pi.L = static_cast<int>(L64);
+  pi.tok0 = tok0;
+  pi.pair_tokens = min(pi.L - tok0, kPairTokens);
+  pi.kv_len = static_cast<int>(kv_len);
+  const int n_keys = pi.kv_len + tok0 + pi.pair_tokens;
+  pi.n_blocks = (n_keys + kBlockKeys - 1) / kBlockKeys;
+  pi.bps = max((pi.n_blocks + p.num_splits - 1) / p.num_splits, kMinBlocksPerSplit);
+  pi.n_active = (pi.n_blocks + pi.bps - 1) / pi.bps;
+  pi.valid = true;
+  return pi;
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     mixed_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -107,43 +218,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sQ = sbase + kOffQ;
   const uint32_t sKV = sbase + kOffKV;
   const uint32_t sP = sbase + kOffP;
+  float2* red = reinterpret_cast<float2*>(smem + kOffRed);
   const Bars bars{sbase + kOffBar};
   uint32_t* tmem_ptr_smem = reinterpret_cast<uint32_t*>(smem + kOffTmemPtr);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  const int h = blockIdx.x % p.num_kv_heads;
+  const int b = blockIdx.x / p.num_kv_heads;
+  const int pair = gridDim.y - 1 - blockIdx.y;
+  const int split = blockIdx.z;
 
-  // ---- sequence bounds (uniform across the CTA) -----------------------------
+  const PairInfo pi = pair_info(p, b, pair, threadIdx.x == 0 && split == 0);
+  if (!pi.valid || split >= pi.n_active) return;
   const int64_t start = p.cu_seqlens[b];
-  const int64_t end = p.cu_seqlens[b + 1];
-  if (start < 0 || end < start || end > p.total_tokens) {
-    if (threadIdx.x == 0) raise_error(CIE_DEVERR_BAD_SEQLENS);
-    return;
-  }
-  const int64_t L64 = end - start;
-  if (tile == 0 && L64 > p.max_seqlen && threadIdx.x == 0) raise_error(CIE_DEVERR_BAD_SEQLENS);
-  const int tok0 = tile * kTileTokens;
-  if (tok0 >= L64) return;
-  const int L = static_cast<int>(L64);
   const int64_t slot = p.slot_ids[b];
-  if (slot < 0 || slot >= p.n_slots) {
-    if (threadIdx.x == 0) raise_error(CIE_DEVERR_BAD_SLOT);
-    return;
-  }
-  int64_t kv_len = p.kv_lens[b];
-  if (kv_len < 0) kv_len = 0;
-  const int tile_tokens = min(L - tok0, kTileTokens);
-  int64_t n_keys64 = kv_len + tok0 + tile_tokens;  // keys visible to the tile's last row
-  if ((kv_len + L + kPage - 1) / kPage > p.bt_stride) {
-    if (threadIdx.x == 0) raise_error(CIE_DEVERR_BAD_LENGTH);
-    return;
-  }
-  const int n_keys = static_cast<int>(n_keys64);
-  const int n_blocks = (n_keys + kBlockKeys - 1) / kBlockKeys;
+  const int blk0 = split * pi.bps;                          // first key block of this CTA
+  const int n_blocks = min(pi.n_blocks, blk0 + pi.bps) - blk0;
+  const int n_keys = pi.kv_len + pi.tok0 + pi.pair_tokens;  // keys of the pair's last row
   const int n_valid_pages = (n_keys + kPage - 1) / kPage;
+  const bool direct = pi.n_active == 1;                     // write O, no partial
+  const int n_tiles = pi.pair_tokens > kTileTokens ? 2 : 1;
+  // rows of tile x that hold a real token: [0, 7 * tokens); quadrants that cover any
+  int n_quads[2];
+  for (int x = 0; x < 2; ++x) {
+    const int tt = x < n_tiles ? min(pi.pair_tokens - x * kTileTokens, kTileTokens) : 0;
+    n_quads[x] = (tt * kGroup + 31) / 32;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -151,21 +252,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bars.kv_empty(s), 1);
     }
     mbar_init(bars.q_full(), 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bars.s_full(i), 1);
-      mbar_init(bars.s_free(i), 128);
-      mbar_init(bars.p_full(i), 128);
-      mbar_init(bars.pv_full(i), 1);
-      mbar_init(bars.pv_free(i), 128);
-    }
     mbar_init(bars.mma_done(), 1);
+    for (int x = 0; x < 2; ++x) {
+      const uint32_t quad_threads = 32u * static_cast<uint32_t>(max(n_quads[x], 1));
+      mbar_init(bars.s_full(x), 1);
+      mbar_init(bars.s_free(x), 2 * quad_threads);
+      mbar_init(bars.p_full(x, 0), quad_threads);
+      mbar_init(bars.p_full(x, 1), quad_threads);
+      mbar_init(bars.pv_done(x, 0), 1);
+      mbar_init(bars.pv_done(x, 1), 1);
+      mbar_init(bars.red_ready(x), 2 * quad_threads);
+    }
     fence_mbar_init();
+    // the merge kernel (programmatic stream serialization) may be scheduled
+    // once every CTA of this grid has started; it waits for our completion
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   }
-  // Q rows 126 and 127 are never loaded: zero them so the tensor core only
-  // ever sees finite values there.
-  if (threadIdx.x < 16) {
-    const uint32_t addr = sQ + kRows * 128 + threadIdx.x * 16;
+  // Rows 126 and 127 of each Q tile are never loaded, and tile B's box is
+  // skipped when the pair has one tile: zero what TMA will not write so the
+  // tensor core only ever sees finite values.
+  if (threadIdx.x < 32) {
+    const int x = threadIdx.x >> 4;
+    const uint32_t addr = sQ + x * kQBytes + kRows * 128 + (threadIdx.x & 15) * 16;
     asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0) : "memory");
+  }
+  if (n_tiles == 1) {
+    for (int e = threadIdx.x; e < kQBytes / 16; e += kThreads)
+      asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(sQ + kQBytes + e * 16),
+                   "r"(0)
+                   : "memory");
   }
   fence_proxy_async_smem();
   if (warp == 1) {
@@ -185,23 +300,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(bars.q_full(), kQLoadBytes);
-      tma_load_4d(sQ, &tm_q, bars.q_full(), 0, 0, h, static_cast<int>(start) + tok0);
+      mbar_arrive_expect_tx(bars.q_full(), n_tiles * kQLoadBytes);
+      tma_load_4d(sQ, &tm_q, bars.q_full(), 0, 0, h, static_cast<int>(start) + pi.tok0);
+      if (n_tiles == 2)
+        tma_load_4d(sQ + kQBytes, &tm_q, bars.q_full(), 0, 0, h,
+                    static_cast<int>(start) + pi.tok0 + kTileTokens);
     }
     const int64_t* bt_row = p.block_table + slot * p.bt_stride;
     for (int j = 0; j < n_blocks; ++j) {
       const int s = j % kStages;
       const uint32_t use = static_cast<uint32_t>(j / kStages);
-      if (lane == 0) {
-        if (j >= kStages && !mbar_wait(bars.kv_empty(s), (use & 1u) ^ 1u, CIE_DEVERR_WAIT_TIMEOUT))
-          ok = false;
-        if (ok) mbar_arrive_expect_tx(bars.kv_full(s), kStageBytes);
-      }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (!ok) break;
+      int page = 0;  // page ids of this block, read before waiting for the stage
       if (lane < kPagesPerBlock) {
-        const int lp = j * kPagesPerBlock + lane;
-        int page = 0;
+        const int lp = (blk0 + j) * kPagesPerBlock + lane;
         if (lp < n_valid_pages) {
           int64_t pid = bt_row[lp];
           if (pid < 0 || pid >= p.n_pages) {
@@ -210,6 +321,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           page = static_cast<int>(pid);
         }
+      }
+      if (lane == 0) {
+        if (j >= kStages && !mbar_wait(bars.kv_empty(s), (use & 1u) ^ 1u, CIE_DEVERR_WAIT_TIMEOUT))
+          ok = false;
+        if (ok) mbar_arrive_expect_tx(bars.kv_full(s), kStageBytes);
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      if (lane < kPagesPerBlock) {
         const uint32_t dst = sKV + s * kStageBytes + lane * kPageBoxBytes;
         tma_load_4d(dst, &tm_k, bars.kv_full(s), 0, 0, h, page);
         tma_load_4d(dst + kKVTileBytes, &tm_v, bars.kv_full(s), 0, 0, h, page);
@@ -227,56 +347,89 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ============================ MMA issuer ==================================
     if (lane == 0) {
       bool ok = mbar_wait(bars.q_full(), 0, CIE_DEVERR_WAIT_TIMEOUT);
-      const uint64_t dq = smem_desc(sQ, 16, 1024);
-      auto issue_pv = [&](int i) -> bool {
-        const int pb = i & 1;
-        const uint32_t use = static_cast<uint32_t>(i >> 1);
-        if (!mbar_wait(bars.p_full(pb), use & 1u, CIE_DEVERR_WAIT_TIMEOUT)) return false;
-        if (i >= 2 && !mbar_wait(bars.pv_free(pb), (use & 1u) ^ 1u, CIE_DEVERR_WAIT_TIMEOUT))
-          return false;
-        tc_fence_after();
-        const int s = i % kStages;
-        const uint32_t v_tile = sKV + s * kStageBytes + kKVTileBytes;
-        const uint32_t p_tile = sP + pb * kPBytes;
-#pragma unroll
-        for (int kk = 0; kk < kBlockKeys / 16; ++kk) {
-          const uint64_t da = smem_desc(p_tile + (kk >> 2) * (kM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t db = smem_desc(v_tile + kk * 2048, kKVTileBytes, 1024);
-          tc_mma_f16(tmem + kColPV + pb * kD, da, db, kIdescPV, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(bars.pv_full(pb));
-        tc_commit(bars.kv_empty(s));
-        return true;
+      auto wait = [&](uint32_t bar, uint32_t parity) {
+        if (ok && !mbar_wait(bar, parity, CIE_DEVERR_WAIT_TIMEOUT)) ok = false;
+        return ok;
       };
-      for (int j = 0; ok && j < n_blocks; ++j) {
-        const int s = j % kStages;
-        const int sb = j & 1;
-        if (!mbar_wait(bars.kv_full(s), static_cast<uint32_t>(j / kStages) & 1u,
-                       CIE_DEVERR_WAIT_TIMEOUT)) {
-          ok = false;
-          break;
-        }
-        if (j >= 2 && !mbar_wait(bars.s_free(sb), (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u,
-                                 CIE_DEVERR_WAIT_TIMEOUT)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t k_tile = sKV + s * kStageBytes;
+      auto issue_s = [&](int x, int j) {  // S_x(j) = Q_x K_j^T
+        const uint32_t k_tile = sKV + (j % kStages) * kStageBytes;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {
-          const uint64_t da = smem_desc(sQ + k * 32, 16, 1024);
+          const uint64_t da = smem_desc(sQ + x * kQBytes + k * 32, 16, 1024);
           const uint64_t db = smem_desc(k_tile + k * 32, 16, 1024);
-          tc_mma_f16(tmem + kColS + sb * kBlockKeys, da, db, kIdescS, k > 0 ? 1u : 0u);
+          tc_mma_f16(tmem + x * 256 + kColS, da, db, kIdescS, k > 0 ? 1u : 0u);
         }
-        (void)dq;
-        tc_commit(bars.s_full(sb));
-        if (j >= 1 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
+        tc_commit(bars.s_full(x));
+      };
+      auto issue_pv = [&](int x, int hh, int j) {  // O_{x,hh} (+)= P_x[:, hh] V_j[hh, :]
+        const uint32_t v_tile = sKV + (j % kStages) * kStageBytes + kKVTileBytes + hh * 8192;
+        const uint32_t p_tile = sP + x * kPBytes + hh * (kM * 128);
+#pragma unroll
+        for (int kk = 0; kk < kHalfKeys / 16; ++kk) {
+          const uint64_t da = smem_desc(p_tile + kk * 32, 16, 1024);
+          const uint64_t db = smem_desc(v_tile + kk * 2048, kKVTileBytes, 1024);
+          tc_mma_f16(tmem + x * 256 + kColO + hh * kD, da, db, kIdescPV,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(bars.pv_done(x, hh));
+      };
+      // Event-driven issue: S_x(j) once K_j is in and tile x has read S_x(j-1);
+      // PV_{x,h}(j) once that half published P_x(j); stage j is released when
+      // every PV of block j is issued. Nothing waits behind an unrelated tile or
+      // half. test_wait never blocks; an idle poll naps briefly so the softmax
+      // warps sharing this SM sub-partition keep their issue slots.
+      int ns[2] = {0, 0};
+      int npv[2][2] = {{0, 0}, {0, 0}};
+      int released = 0;
+      const int n_halves = 2 * n_tiles;
+      int pv_left = n_blocks * n_halves;
+      unsigned long long idle_since = 0;
+      while (ok && (pv_left > 0 || released < n_blocks)) {
+        bool progress = false;
+        for (int x = 0; x < n_tiles; ++x) {
+          const int j = ns[x];
+          if (j < n_blocks &&
+              mbar_test(bars.kv_full(j % kStages), static_cast<uint32_t>(j / kStages) & 1u) &&
+              (j == 0 || mbar_test(bars.s_free(x), static_cast<uint32_t>(j - 1) & 1u))) {
+            tc_fence_after();
+            issue_s(x, j);
+            ns[x] = j + 1;
+            progress = true;
+          }
+        }
+        for (int x = 0; x < n_tiles; ++x) {
+          for (int hh = 0; hh < 2; ++hh) {
+            const int j = npv[x][hh];
+            if (j < ns[x] && mbar_test(bars.p_full(x, hh), static_cast<uint32_t>(j) & 1u)) {
+              tc_fence_after();
+              issue_pv(x, hh, j);
+              npv[x][hh] = j + 1;
+              --pv_left;
+              progress = true;
+            }
+          }
+        }
+        while (released < n_blocks) {
+          bool all = true;
+          for (int x = 0; x < n_tiles; ++x) all = all && npv[x][0] > released && npv[x][1] > released;
+          if (!all) break;
+          tc_commit(bars.kv_empty(released % kStages));
+          ++released;
+          progress = true;
+        }
+        if (progress) {
+          idle_since = 0;
+        } else {
+          const unsigned long long now = global_timer_ns();
+          if (idle_since == 0) idle_since = now;
+          else if (now - idle_since > kWaitLimitNs) {
+            raise_error(CIE_DEVERR_WAIT_TIMEOUT);
+            ok = false;
+          }
+          __nanosleep(32);
         }
       }
-      if (ok && n_blocks > 0) issue_pv(n_blocks - 1);
+      (void)wait;
       // drain: every MMA this thread issued has completed before TMEM is freed
       tc_commit(bars.mma_done());
       mbar_wait(bars.mma_done(), 0, CIE_DEVERR_WAIT_TIMEOUT);
@@ -284,140 +437,206 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ============================ softmax =====================================
+    const int sw = warp - 2;                // 0..15
+    const int x = sw >> 3;                  // tile
+    const int half = (sw >> 2) & 1;         // key columns [64*half, 64*half + 64)
     const int quad = warp & 3;              // TMEM lane quadrant of this warp
     const int row = quad * 32 + lane;       // tile row == TMEM lane
-    const int tok_in_tile = row / kGroup;
-    const int head_in_group = row - tok_in_tile * kGroup;
-    const bool row_valid = row < kRows && tok_in_tile < tile_tokens;
-    // inclusive causal limit of this row; padded rows use the tile's first
-    // row limit so that every value they produce stays finite
-    const int limit = static_cast<int>(kv_len) + tok0 + (row_valid ? tok_in_tile : 0);
-    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    constexpr float kScale = 0.125f;  // head_dim ** -0.5 for D = 64
+    if (x < n_tiles && quad < n_quads[x]) {
+      const int tile_tok0 = pi.tok0 + x * kTileTokens;
+      const int tile_tokens = min(pi.L - tile_tok0, kTileTokens);
+      const int tok_in_tile = row / kGroup;
+      const int head_in_group = row - tok_in_tile * kGroup;
+      const bool row_valid = row < kRows && tok_in_tile < tile_tokens;
+      // inclusive causal limit (absolute key index) of this row; padding rows
+      // use the tile's first row limit so that every value stays finite
+      const int limit = pi.kv_len + tile_tok0 + (row_valid ? tok_in_tile : 0);
+      const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+      const uint32_t t_s = tmem + lane_addr + x * 256 + kColS + half * kHalfKeys;
+      const uint32_t t_o = tmem + lane_addr + x * 256 + kColO + half * kD;
+      const uint32_t p_tile = sP + x * kPBytes + half * (kM * 128);
+      constexpr float kScale = 0.125f;  // head_dim ** -0.5 for D = 64
+      const float2 c2 = make_float2(kScale * kLog2e, kScale * kLog2e);
 
-    float m_run = -CUDART_INF_F;
-    float l_run = 0.f;
-    float alpha_prev = 1.f;
-    float o_acc[kD];
-#pragma unroll
-    for (int d = 0; d < kD; ++d) o_acc[d] = 0.f;
-
-    auto fold_pv = [&](int i, float alpha) -> bool {
-      const int pb = i & 1;
-      if (!mbar_wait(bars.pv_full(pb), static_cast<uint32_t>(i >> 1) & 1u, CIE_DEVERR_WAIT_TIMEOUT))
-        return false;
-      tc_fence_after();
-      uint32_t r0[32], r1[32];
-      tmem_ld_32x32b_x32(tmem + lane_addr + kColPV + pb * kD, r0);
-      tmem_ld_32x32b_x32(tmem + lane_addr + kColPV + pb * kD + 32, r1);
-      tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bars.pv_free(pb));
-#pragma unroll
-      for (int d = 0; d < 32; ++d) {
-        o_acc[d] = o_acc[d] * alpha + __uint_as_float(r0[d]);
-        o_acc[32 + d] = o_acc[32 + d] * alpha + __uint_as_float(r1[d]);
-      }
-      return true;
-    };
-
-    bool ok = true;
-    for (int j = 0; j < n_blocks; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(bars.s_full(sb), static_cast<uint32_t>(j >> 1) & 1u, CIE_DEVERR_WAIT_TIMEOUT)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sr[kBlockKeys];
-#pragma unroll
-      for (int c = 0; c < kBlockKeys / 32; ++c)
-        tmem_ld_32x32b_x32(tmem + lane_addr + kColS + sb * kBlockKeys + c * 32,
-                           *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
-      tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bars.s_free(sb));
-
-      const int lim = limit - j * kBlockKeys;  // last visible column of this block
-      float mx = -CUDART_INF_F;
-      if (lim >= kBlockKeys - 1) {
-#pragma unroll
-        for (int c = 0; c < kBlockKeys; ++c) {
-          const float x = __uint_as_float(sr[c]) * kScale;
-          sr[c] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+      float m_ref = -CUDART_INF_F;  // scaled max the P values of this half are taken against
+      float l_run = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n_blocks; ++j) {
+        const uint32_t par = static_cast<uint32_t>(j) & 1u;
+        if (!__all_sync(0xffffffffu, mbar_wait(bars.s_full(x), par, CIE_DEVERR_WAIT_TIMEOUT))) {
+          ok = false;
+          break;
         }
-      } else {
-#pragma unroll
-        for (int c = 0; c < kBlockKeys; ++c) {
-          const float x = c <= lim ? __uint_as_float(sr[c]) * kScale : -CUDART_INF_F;
-          sr[c] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
-      }
-      const float m_new = fmaxf(m_run, mx);  // finite: key 0 is visible to every row
-      const float alpha = ex2((m_run - m_new) * kLog2e);
-      const float mneg = m_new * kLog2e;
-      float ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, ls3 = 0.f;
-      const uint32_t p_tile = sP + sb * kPBytes;
-#pragma unroll
-      for (int c8 = 0; c8 < kBlockKeys / 8; ++c8) {
-        float pv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          pv[e] = ex2(fmaf(__uint_as_float(sr[c8 * 8 + e]), kLog2e, -mneg));
-        ls0 += pv[0] + pv[4];
-        ls1 += pv[1] + pv[5];
-        ls2 += pv[2] + pv[6];
-        ls3 += pv[3] + pv[7];
-        const uint32_t w0 = pack_half2(pv[0], pv[1]);
-        const uint32_t w1 = pack_half2(pv[2], pv[3]);
-        const uint32_t w2 = pack_half2(pv[4], pv[5]);
-        const uint32_t w3 = pack_half2(pv[6], pv[7]);
-        // K-major, 128B swizzle: keys [64a, 64a+64) of all rows form atom column a
-        const uint32_t addr = p_tile + (c8 >> 3) * (kM * 128) + sw128(row, c8 & 7);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0), "r"(w1),
-                     "r"(w2), "r"(w3)
-                     : "memory");
-      }
-      l_run = l_run * alpha + ((ls0 + ls1) + (ls2 + ls3));
-      m_run = m_new;
+        tc_fence_after();
+        uint32_t sr[kHalfKeys];
+        tmem_ld_32x32b_x32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tmem_ld_32x32b_x32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        tc_wait_ld();
+        tc_fence_before();
+        mbar_arrive(bars.s_free(x));
 
-      // V rows past the last key of the tile hold stale pool data: zero them
-      // (each softmax thread owns one V row of the block) so that
-      // 0 * (non-finite) cannot reach the accumulator.
-      if (j == n_blocks - 1 && j * kBlockKeys + row >= n_keys) {
-        const uint32_t vrow = sKV + (j % kStages) * kStageBytes + kKVTileBytes;
+        // raw max over my 64 columns of this block; masked columns become -inf
+        const int lim = limit - (blk0 + j) * kBlockKeys - half * kHalfKeys;
+        float mx8[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(vrow + sw128(row, c)),
-                       "r"(0)
+        for (int e = 0; e < 8; ++e) mx8[e] = -CUDART_INF_F;
+        if (lim >= kHalfKeys - 1) {
+#pragma unroll
+          for (int c = 0; c < kHalfKeys; ++c)
+            mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sr[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < kHalfKeys; ++c) {
+            const float v = c <= lim ? __uint_as_float(sr[c]) : -CUDART_INF_F;
+            sr[c] = __float_as_uint(v);
+            mx8[c & 7] = fmaxf(mx8[c & 7], v);
+          }
+        }
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
+                         kScale;
+
+        // Move the reference max only when this block's max exceeds it by more
+        // than 2^8 (then l and O_h are rescaled by alpha). The exponentials go
+        // to registers first; the wait for PV(j-1) of this half, which must
+        // have consumed P(j-1) and updated O_h, comes only before P and O move.
+        const bool need = mx > m_ref + kRescaleLog2 / kLog2e;
+        const float alpha = (need && j > 0) ? ex2((m_ref - mx) * kLog2e) : 1.f;
+        if (need) m_ref = mx;
+        // no visible key in this half yet: every column is -inf and p = 0
+        const float mneg = m_ref == -CUDART_INF_F ? 0.f : -m_ref * kLog2e;
+        const float2 mneg2 = make_float2(mneg, mneg);
+        float2 lsum0 = make_float2(0.f, 0.f), lsum1 = make_float2(0.f, 0.f);
+        uint32_t pw[kHalfKeys / 2];
+#pragma unroll
+        for (int c8 = 0; c8 < kHalfKeys / 8; ++c8) {
+          float pv[8];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const float2 t = __ffma2_rn(make_float2(__uint_as_float(sr[c8 * 8 + e]),
+                                                    __uint_as_float(sr[c8 * 8 + e + 1])),
+                                        c2, mneg2);
+            pv[e] = ex2(t.x);
+            pv[e + 1] = ex2(t.y);
+          }
+          lsum0 = __fadd2_rn(lsum0, __fadd2_rn(make_float2(pv[0], pv[1]), make_float2(pv[4], pv[5])));
+          lsum1 = __fadd2_rn(lsum1, __fadd2_rn(make_float2(pv[2], pv[3]), make_float2(pv[6], pv[7])));
+          pw[c8 * 4 + 0] = pack_half2(pv[0], pv[1]);
+          pw[c8 * 4 + 1] = pack_half2(pv[2], pv[3]);
+          pw[c8 * 4 + 2] = pack_half2(pv[4], pv[5]);
+          pw[c8 * 4 + 3] = pack_half2(pv[6], pv[7]);
+        }
+        l_run = l_run * alpha + ((lsum0.x + lsum0.y) + (lsum1.x + lsum1.y));
+
+        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(bars.pv_done(x, half), par ^ 1u,
+                                                         CIE_DEVERR_WAIT_TIMEOUT))) {
+          ok = false;
+          break;
+        }
+        // TMEM round trip of O_h by the whole warp when any of its rows moved
+        // its max; the other rows multiply by 1. O_h holds nothing before the
+        // first PV of this CTA (j == 0).
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < kD; c += 16) {  // 16 columns at a time: few live registers
+            uint32_t o[16];
+            tmem_ld_32x32b_x16(t_o + c, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int d = 0; d < 16; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
+            tmem_st_32x32b_x16(t_o + c, o);
+          }
+          tc_wait_st();
+          tc_fence_before();
+        }
+#pragma unroll
+        for (int c8 = 0; c8 < kHalfKeys / 8; ++c8) {
+          // K-major, 128B swizzle: keys [64*half, 64*half+64) form atom column `half`
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(p_tile + sw128(row, c8)),
+                       "r"(pw[c8 * 4 + 0]), "r"(pw[c8 * 4 + 1]), "r"(pw[c8 * 4 + 2]),
+                       "r"(pw[c8 * 4 + 3])
                        : "memory");
         }
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(bars.p_full(sb));
 
-      if (j >= 1 && !fold_pv(j - 1, alpha_prev)) {
-        ok = false;
-        break;
+        // V rows past the pair's last key hold stale pool data: zero them so
+        // that 0 * (non-finite) cannot reach an accumulator. The working
+        // threads of (tile x, key half h) zero the stale rows among V rows
+        // [64h, 64h + 64) before their p_full arrival below, so PV(x, h) reads
+        // zeros; both tiles do it (the same zeros) because their PVs are
+        // issued independently.
+        if (blk0 + j == pi.n_blocks - 1) {
+          const int first = max(n_keys - (blk0 + j) * kBlockKeys, half * kHalfKeys);
+          const int rows = (half + 1) * kHalfKeys - first;
+          if (rows > 0) {
+            const uint32_t vtile = sKV + (j % kStages) * kStageBytes + kKVTileBytes;
+            const int nthr = 32 * n_quads[x];
+            for (int e = quad * 32 + lane; e < rows * 8; e += nthr) {
+              asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(
+                               vtile + sw128(first + (e >> 3), e & 7)),
+                           "r"(0)
+                           : "memory");
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(bars.p_full(x, half));
       }
-      alpha_prev = alpha;
-    }
-    if (ok && n_blocks > 0) ok = fold_pv(n_blocks - 1, alpha_prev);
-
-    if (ok && row_valid) {
-      const float inv = 1.f / l_run;
-      const int64_t tok = start + tok0 + tok_in_tile;
-      __half* dst = p.o + (tok * p.num_q_heads + h * kGroup + head_in_group) * kD;
+      // last PV of this half, then combine the two halves of the row
+      if (ok && n_blocks > 0)
+        ok = __all_sync(0xffffffffu, mbar_wait(bars.pv_done(x, half),
+                                               static_cast<uint32_t>(n_blocks - 1) & 1u,
+                                               CIE_DEVERR_WAIT_TIMEOUT));
+      red[(x * 2 + half) * kM + row] = make_float2(m_ref, l_run);
+      mbar_arrive(bars.red_ready(x));
+      mbar_wait(bars.red_ready(x), 0, CIE_DEVERR_WAIT_TIMEOUT);
+      const float2 a = red[(x * 2 + 0) * kM + row];
+      const float2 c = red[(x * 2 + 1) * kM + row];
+      const float M = fmaxf(a.x, c.x);
+      const float w0 = a.x == -CUDART_INF_F ? 0.f : ex2((a.x - M) * kLog2e);
+      const float w1 = c.x == -CUDART_INF_F ? 0.f : ex2((c.x - M) * kLog2e);
+      const float l_tot = a.y * w0 + c.y * w1;
+      // this thread produces output columns [32*half, 32*half + 32) of its row
+      tc_fence_after();
+      float out[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 w;
-        w.x = pack_half2(o_acc[c * 8 + 0] * inv, o_acc[c * 8 + 1] * inv);
-        w.y = pack_half2(o_acc[c * 8 + 2] * inv, o_acc[c * 8 + 3] * inv);
-        w.z = pack_half2(o_acc[c * 8 + 4] * inv, o_acc[c * 8 + 5] * inv);
-        w.w = pack_half2(o_acc[c * 8 + 6] * inv, o_acc[c * 8 + 7] * inv);
-        reinterpret_cast<uint4*>(dst)[c] = w;
+      for (int c16 = 0; c16 < 2; ++c16) {
+        uint32_t o0[16], o1[16];
+        const uint32_t col = half * 32 + c16 * 16;
+        tmem_ld_32x32b_x16(tmem + lane_addr + x * 256 + kColO + col, o0);
+        tmem_ld_32x32b_x16(tmem + lane_addr + x * 256 + kColO + kD + col, o1);
+        tc_wait_ld();
+#pragma unroll
+        for (int d = 0; d < 16; ++d)
+          out[c16 * 16 + d] = __uint_as_float(o0[d]) * w0 + __uint_as_float(o1[d]) * w1;
+      }
+      if (ok && row_valid) {
+        const int64_t tok = start + tile_tok0 + tok_in_tile;
+        const int hq = h * kGroup + head_in_group;
+        if (direct) {
+          const float inv = 1.f / l_tot;
+          __half* dst = p.o + (tok * p.num_q_heads + hq) * kD + half * 32;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint4 w;
+            w.x = pack_half2(out[cc * 8 + 0] * inv, out[cc * 8 + 1] * inv);
+            w.y = pack_half2(out[cc * 8 + 2] * inv, out[cc * 8 + 3] * inv);
+            w.z = pack_half2(out[cc * 8 + 4] * inv, out[cc * 8 + 5] * inv);
+            w.w = pack_half2(out[cc * 8 + 6] * inv, out[cc * 8 + 7] * inv);
+            reinterpret_cast<uint4*>(dst)[cc] = w;
+          }
+        } else {
+          float* rec = p.part + ((static_cast<int64_t>(split) * p.total_tokens + tok) *
+                                     p.num_q_heads + hq) * kPartFloats;
+#pragma unroll
+          for (int cc = 0; cc < 16; ++cc)
+            reinterpret_cast<float2*>(rec + half * 32)[cc] =
+                make_float2(out[cc * 2 + 0], out[cc * 2 + 1]);
+          if (half == 0) {
+            rec[kD] = M;  // -inf when this key range had no visible key for the row
+            rec[kD + 1] = l_tot;
+          }
+        }
       }
     }
   }
@@ -428,17 +647,92 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+// Combines the key-range partials of the tile pairs that were split: per row,
+// O = sum_s w_s acc_s / sum_s w_s l_s with w_s = exp(m_s - max m). One warp per
+// row (blockIdx.z picks 8 rows of the pair): lane s < splits loads (m_s, l_s)
+// so the maximum and the denominator are warp reductions, then every lane
+// accumulates two output columns over the splits. Launched with programmatic
+// stream serialization: griddepcontrol.wait holds it until the attention
+// kernel has finished and its writes are visible.
+__global__ void __launch_bounds__(256) mixed_merge_kernel(const Params p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int h = blockIdx.x % p.num_kv_heads;
+  const int b = blockIdx.x / p.num_kv_heads;
+  const int pair = blockIdx.y;
+  const PairInfo pi = pair_info(p, b, pair, false);
+  if (!pi.valid || pi.n_active <= 1) return;
+  const int r = blockIdx.z * 8 + (threadIdx.x >> 5);
+  if (r >= pi.pair_tokens * kGroup) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = p.cu_seqlens[b] + pi.tok0 + r / kGroup;
+  const int hq = h * kGroup + r % kGroup;
+  const int64_t split_stride = p.total_tokens * p.num_q_heads * kPartFloats;
+  const float* rec0 = p.part + (tok * p.num_q_heads + hq) * kPartFloats;
+  float m = -CUDART_INF_F, l = 0.f;
+  if (lane < pi.n_active) {
+    m = rec0[lane * split_stride + kD];
+    l = rec0[lane * split_stride + kD + 1];
+  }
+  float M = m;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float w = (lane < pi.n_active && m != -CUDART_INF_F) ? ex2((m - M) * kLog2e) : 0.f;
+  float den = w * l;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+  float2 num = make_float2(0.f, 0.f);
+  for (int s = 0; s < pi.n_active; ++s) {
+    const float ws = __shfl_sync(0xffffffffu, w, s);
+    if (ws == 0.f) continue;
+    const float2 a = *reinterpret_cast<const float2*>(rec0 + s * split_stride + 2 * lane);
+    num.x += ws * a.x;
+    num.y += ws * a.y;
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  *reinterpret_cast<__half2*>(p.o + (tok * p.num_q_heads + hq) * kD + 2 * lane) =
+      __floats2half2_rn(num.x * inv, num.y * inv);
+}
+
 }  // namespace mixed
 }  // namespace cie
 
-extern "C" int cie_mixed_attention(const void* q, const void* k, const void* v,
-                                   int64_t max_seqlen, const int64_t* cu_seqlens,
-                                   const int64_t* kv_lens, const int64_t* slot_ids,
-                                   const int64_t* block_table, void* o, int batch,
-                                   int64_t total_tokens, int num_q_heads, int num_kv_heads,
-                                   int head_dim, int page_size, int64_t n_pages, int64_t n_slots,
-                                   int64_t bt_stride, int64_t kv_page_stride,
-                                   int64_t kv_head_stride, cie_stream_t stream) {
+extern "C" {
+
+int cie_mixed_default_splits(int batch, int64_t total_tokens, int num_kv_heads, int device) {
+  using namespace cie::mixed;
+  int sms = 148;
+  if (device >= 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && n > 0)
+      sms = n;
+  }
+  if (batch <= 0 || total_tokens <= 0 || num_kv_heads <= 0) return 1;
+  // Tile-pair CTAs without splitting: at least one per non-empty sequence and
+  // one per 36 tokens. A CTA pays a fixed pipeline fill, so key ranges are
+  // split only while the grid would leave SMs idle.
+  const int64_t pairs = (total_tokens + kPairTokens - 1) / kPairTokens;
+  const int64_t units = static_cast<int64_t>(num_kv_heads) * (pairs > batch ? pairs : batch);
+  int64_t s = sms / units;
+  if (s < 1) s = 1;
+  if (s > kMaxSplits) s = kMaxSplits;
+  return static_cast<int>(s);
+}
+
+size_t cie_mixed_workspace_bytes(int64_t total_tokens, int num_q_heads, int head_dim,
+                                 int num_splits) {
+  if (total_tokens <= 0 || num_splits <= 1 || num_q_heads <= 0 || head_dim <= 0) return 0;
+  return static_cast<size_t>(num_splits) * static_cast<size_t>(total_tokens) * num_q_heads *
+         (static_cast<size_t>(head_dim) + 2) * sizeof(float);
+}
+
+int cie_mixed_attention(const void* q, const void* k, const void* v, int64_t max_seqlen,
+                        const int64_t* cu_seqlens, const int64_t* kv_lens,
+                        const int64_t* slot_ids, const int64_t* block_table, void* o,
+                        void* workspace, size_t workspace_bytes, int batch,
+                        int64_t total_tokens, int num_q_heads, int num_kv_heads, int head_dim,
+                        int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                        int64_t kv_page_stride, int64_t kv_head_stride, int num_splits,
+                        cie_stream_t stream) {
   using namespace cie;
   using namespace cie::mixed;
   if (batch < 0 || total_tokens < 0 || max_seqlen < 0)
@@ -457,15 +751,28 @@ extern "C" int cie_mixed_attention(const void* q, const void* k, const void* v,
   if (n_pages >= (int64_t(1) << 31) || total_tokens >= (int64_t(1) << 31) ||
       bt_stride * kPage >= (int64_t(1) << 31))
     return fail(CIE_ERR_OVERFLOW, "n_pages / total_tokens / keys per slot must fit int32");
-  if (batch > 65535 || num_kv_heads > 65535)
-    return fail(CIE_ERR_UNSUPPORTED, "batch %d / kv heads %d", batch, num_kv_heads);
+  const int64_t n_pairs = (max_seqlen + kPairTokens - 1) / kPairTokens;
+  if (n_pairs > 65535)
+    return fail(CIE_ERR_UNSUPPORTED, "max_seqlen %lld needs more than 65535 query tile pairs",
+                (long long)max_seqlen);
+  if (static_cast<int64_t>(batch) * num_kv_heads > 0x7fffffff)
+    return fail(CIE_ERR_OVERFLOW, "batch x kv heads does not fit the grid");
   if (kv_head_stride < page_size * head_dim || kv_page_stride < kv_head_stride * num_kv_heads)
     return fail(CIE_ERR_INVALID_ARGUMENT, "overlapping K/V strides");
   if ((kv_page_stride % 8) || (kv_head_stride % 8) || !aligned16(k) || !aligned16(v) ||
       !aligned16(q) || !aligned16(o))
     return fail(CIE_ERR_ALIGNMENT, "q/o/k/v must be 16-byte aligned with 16-byte strides");
-  const int64_t n_tiles = (max_seqlen + kTileTokens - 1) / kTileTokens;
-  if (n_tiles > 0x7fffffff) return fail(CIE_ERR_OVERFLOW, "max_seqlen too large");
+  const int S = num_splits > 0 ? num_splits
+                               : cie_mixed_default_splits(batch, total_tokens, num_kv_heads,
+                                                          current_device());
+  if (S > kMaxSplits) return fail(CIE_ERR_INVALID_ARGUMENT, "num_splits %d > %d", S, kMaxSplits);
+  if (S > 1) {
+    const size_t need = cie_mixed_workspace_bytes(total_tokens, num_q_heads, head_dim, S);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(CIE_ERR_WORKSPACE, "split path needs %zu workspace bytes, got %zu", need,
+                  workspace == nullptr ? size_t(0) : workspace_bytes);
+    if (!aligned16(workspace)) return fail(CIE_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+  }
 
   CUtensorMap tm_q, tm_k, tm_v;
   {
@@ -501,16 +808,37 @@ extern "C" int cie_mixed_attention(const void* q, const void* k, const void* v,
   p.slot_ids = slot_ids;
   p.block_table = block_table;
   p.o = static_cast<__half*>(o);
+  p.part = S > 1 ? static_cast<float*>(workspace) : nullptr;
   p.total_tokens = total_tokens;
   p.max_seqlen = max_seqlen;
   p.n_pages = n_pages;
   p.n_slots = n_slots;
   p.bt_stride = bt_stride;
   p.num_q_heads = num_q_heads;
-  dim3 grid(static_cast<unsigned>(n_tiles), num_kv_heads, batch);
-  mixed_attention_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
-      tm_q, tm_k, tm_v, p);
+  p.num_kv_heads = num_kv_heads;
+  p.num_splits = S;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // x: (sequence, kv head); y: tile pair, walked last-pair-first; z: key range
+  dim3 grid(static_cast<unsigned>(batch * num_kv_heads), static_cast<unsigned>(n_pairs), S);
+  mixed_attention_kernel<<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "mixed launch: %s", cudaGetErrorString(e));
+  if (S > 1) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(batch * num_kv_heads), static_cast<unsigned>(n_pairs),
+                       (2 * kRows + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, mixed_merge_kernel, p);
+    if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "mixed merge launch: %s", cudaGetErrorString(e));
+  }
   return CIE_OK;
 }
+
+}  // extern "C"

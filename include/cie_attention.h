@@ -123,8 +123,16 @@ int cie_decode_attention_noalloc(const void* q, const void* k, const void* v,
 
 /* ---- varlen mixed (chunked prefill + decode) attention --------------------- */
 
+/* Key-range splits used when cie_mixed_attention() is given num_splits <= 0:
+ * 1 unless the tile pairs alone would leave SMs of `device` idle. */
+int cie_mixed_default_splits(int batch, int64_t total_tokens, int num_kv_heads, int device);
+
+/* Bytes of fp32 workspace the split path needs (0 when num_splits == 1). */
+size_t cie_mixed_workspace_bytes(int64_t total_tokens, int num_q_heads, int head_dim,
+                                 int num_splits);
+
 /*
- * Causal attention for a batch of chunks in one launch.
+ * Causal attention for a batch of chunks in one call.
  * Replaces attn/core.py:69-111 (mixed_gqa_attention) and its kernel
  * kernels/prefill_attention.py:10-198; body of inference::gqa_mixed_attention
  * (attn/core.py:128-137).
@@ -133,13 +141,18 @@ int cie_decode_attention_noalloc(const void* q, const void* k, const void* v,
  *   of slot slot_ids[b] (the chunk's own K/V are already in the pool).
  *   max_seqlen bounds every chunk length (the bucket's token count).
  *   Rows outside every [cu_seqlens[b], cu_seqlens[b+1]) are not written.
+ * num_splits: key ranges per tile pair (<= 0: cie_mixed_default_splits,
+ * at most 16); with more than one, partials go to `workspace`
+ * (>= cie_mixed_workspace_bytes(...), 16-byte aligned) and a second kernel
+ * merges them.
  */
 int cie_mixed_attention(const void* q, const void* k, const void* v, int64_t max_seqlen,
                         const int64_t* cu_seqlens, const int64_t* kv_lens,
                         const int64_t* slot_ids, const int64_t* block_table, void* o,
-                        int batch, int64_t total_tokens, int num_q_heads, int num_kv_heads,
-                        int head_dim, int page_size, int64_t n_pages, int64_t n_slots,
-                        int64_t bt_stride, int64_t kv_page_stride, int64_t kv_head_stride,
+                        void* workspace, size_t workspace_bytes, int batch,
+                        int64_t total_tokens, int num_q_heads, int num_kv_heads, int head_dim,
+                        int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                        int64_t kv_page_stride, int64_t kv_head_stride, int num_splits,
                         cie_stream_t stream);
 
 /* ---- KV-page scatter ------------------------------------------------------- */

@@ -76,12 +76,22 @@ def test_decode_empty_batch_is_a_no_op():
 def test_mixed_and_update_argument_checks():
     lib = native.lib()
     p = 1 << 20
-    assert lib.cie_mixed_attention(p, p, p, 16, p, p, p, p, p, 2, 16, 14, 2, 128, 16, 10, 3, 10,
-                                   4096, 2048, None) == -2
-    assert lib.cie_mixed_attention(None, p, p, 16, p, p, p, p, p, 2, 16, 14, 2, 64, 16, 10, 3,
-                                   10, 2048, 1024, None) == -1
-    assert lib.cie_mixed_attention(p, p, p, 0, p, p, p, p, p, 2, 16, 14, 2, 64, 16, 10, 3, 10,
-                                   2048, 1024, None) == 0
+    def mixed(**kw):
+        a = dict(q=p, k=p, v=p, max_seqlen=16, cu=p, kvl=p, slots=p, bt=p, o=p, ws=None,
+                 ws_bytes=0, batch=2, T=16, hq=14, hkv=2, d=64, page=16, n_pages=10, n_slots=3,
+                 bt_stride=10, pstride=2048, hstride=1024, splits=1, stream=None)
+        a.update(kw)
+        return lib.cie_mixed_attention(*a.values())
+    assert mixed(d=128) == -2
+    assert mixed(q=None) == -1
+    assert mixed(max_seqlen=0) == 0
+    assert mixed(splits=4) == -5                 # split path without workspace
+    assert mixed(splits=17) == -1
+    assert lib.cie_mixed_workspace_bytes(2048, 14, 64, 1) == 0
+    assert lib.cie_mixed_workspace_bytes(2048, 14, 64, 3) == 3 * 2048 * 14 * 66 * 4
+    assert lib.cie_mixed_default_splits(4, 2048, 2, -1) == 1
+    assert lib.cie_mixed_default_splits(32, 32, 2, -1) == 2
+    assert lib.cie_mixed_default_splits(1, 1, 2, -1) == 16
     assert lib.cie_kv_mixed_update(None, p, p, p, p, p, 4, 2, 64, 16, 10, 2048, 1024, 1152, 64,
                                    1152, 64, None) == -1
     assert lib.cie_kv_decode_update(p, p, p, p, p, p, p, 4, 2, 64, 16, 10, 3, 10, 100, 1024,

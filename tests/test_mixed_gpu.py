@@ -48,12 +48,12 @@ def torch_mixed_fp32(c):
     return out.to(torch.float16)
 
 
-def _run(c, sentinel=None):
+def _run(c, sentinel=None, splits=0):
     out = None
     if sentinel is not None:
         out = torch.full_like(c.q, sentinel)
     return cabi.mixed_attention(c.q, c.k, c.v, c.max_seqlen, c.cu_seqlens, c.kv_lens,
-                                c.slot_ids, c.block_table, out=out)
+                                c.slot_ids, c.block_table, out=out, num_splits=splits)
 
 
 @pytest.fixture(autouse=True)
@@ -70,11 +70,12 @@ def _case_from_golden(g, dev):
                        block_table=g["block_table"].to(dev))
 
 
+@pytest.mark.parametrize("splits", [1, 3, 16, 0])
 @pytest.mark.parametrize("name", ["mixed_small", "mixed_edges", "mixed_config3_small"])
-def test_golden_cases_cabi(name, cuda_device):
+def test_golden_cases_cabi(name, splits, cuda_device):
     g = load_golden(name)
     c = _case_from_golden(g, cuda_device)
-    o = _run(c, sentinel=7.0)
+    o = _run(c, sentinel=7.0, splits=splits)
     rows = oracle.valid_token_rows(g["cu_seqlens"], g["q"].shape[1])
     assert _maxabs(o[0, rows.to(cuda_device)], g["out"][0, rows]) <= TOL
     ref = oracle.mixed_attention_fp32(g["q"], g["k"], g["v"], int(g["max_seqlen"]),
@@ -98,8 +99,9 @@ def test_edge_shapes(chunks, kvs, cuda_device):
                                       c.slot_ids, c.block_table)
     cd = W.MixedCase(**{f: (getattr(c, f).to(cuda_device) if torch.is_tensor(getattr(c, f))
                             else getattr(c, f)) for f in c.__dataclass_fields__})
-    o = _run(cd)
-    assert _maxabs(o, ref) <= TOL
+    for splits in (1, 4, 0):
+        o = _run(cd, splits=splits)
+        assert _maxabs(o, ref) <= TOL
 
 
 def test_config3_full(cuda_device):
@@ -107,9 +109,10 @@ def test_config3_full(cuda_device):
     c = W.make_mixed_case(chunk, kv, seed=0, device=cuda_device, max_seqlen=2048,
                           generate_on_device=True)
     ref = torch_mixed_fp32(c)
-    o = _run(c)
-    assert torch.isfinite(o.float()).all()
-    assert _maxabs(o, ref) <= TOL
+    for splits in (0, 1, 5):
+        o = _run(c, splits=splits)
+        assert torch.isfinite(o.float()).all()
+        assert _maxabs(o, ref) <= TOL
 
 
 def test_512_token_chunks(cuda_device):
@@ -117,8 +120,9 @@ def test_512_token_chunks(cuda_device):
     kv = torch.randint(0, 8193, (4,), generator=g).tolist()
     c = W.make_mixed_case([512] * 4, kv, seed=1, device=cuda_device, generate_on_device=True)
     ref = torch_mixed_fp32(c)
-    o = _run(c)
-    assert _maxabs(o, ref) <= TOL
+    for splits in (0, 1, 8):
+        o = _run(c, splits=splits)
+        assert _maxabs(o, ref) <= TOL
 
 
 def test_nonfinite_stale_rows_do_not_leak(cuda_device):
@@ -141,8 +145,9 @@ def test_nonfinite_stale_rows_do_not_leak(cuda_device):
     cd = W.MixedCase(q=c.q.to(dev), k=k.to(dev), v=v.to(dev), max_seqlen=c.max_seqlen,
                      cu_seqlens=c.cu_seqlens.to(dev), kv_lens=c.kv_lens.to(dev),
                      slot_ids=c.slot_ids.to(dev), block_table=c.block_table.to(dev))
-    o = _run(cd)
-    assert _maxabs(o, ref) <= TOL
+    for splits in (1, 2):
+        o = _run(cd, splits=splits)
+        assert _maxabs(o, ref) <= TOL
 
 
 def test_torch_op_matches_cabi_bitwise(cuda_device):
