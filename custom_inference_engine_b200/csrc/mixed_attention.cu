@@ -14,32 +14,35 @@
 // over several CTAs, each writes an fp32 partial (m, l, unnormalised O) per
 // row and a merge kernel combines them; a pair that is not split writes O.
 //
-// Warp roles (576 threads):
+// Tensor memory (512 columns) per tile x: S = Q K^T at 256x (128 fp32
+// columns), P at 256x + 128 (128 fp16 keys packed two per column) and the
+// O accumulator at 256x + 192 (64 columns). P never touches shared memory:
+// the softmax writes it with tcgen05.st and O += P V reads it as the
+// TMEM-resident A operand, with V from shared memory.
+//
+// Warp roles (384 threads, three warpgroups):
 //   warp 0       TMA producer: both Q tiles, then per key block the 8 K and
 //                8 V pages of this kv head (2 KiB boxes through the block
-//                table) into a 3-stage ring.
+//                table) into a 5-stage ring.
 //   warp 1       TMEM owner and single-thread, event-driven MMA issuer:
-//                S_x(j+1) = Q_x K_{j+1}^T as soon as K_{j+1} is in and tile x's
-//                softmax has read S_x(j); PV for each (tile, key half) as soon
-//                as that half of P_x(j) is published. The next QK^T therefore
-//                runs while the softmax works on this block, and no tile or
-//                half waits behind another.
-//   warps 2-9    softmax of tile A, warps 10-17 of tile B: two warps per TMEM
-//                lane quadrant, one for key columns 0-63 of every block, one
-//                for 64-127. Each half keeps its OWN online softmax (reference
-//                max m, sum l) and its own O accumulator in TMEM
-//                (O_h += P[:, half] V[half, :], issued per half), so the two
-//                halves never synchronise inside the key loop; they are
-//                combined once at the end like two split-KV partials. The
-//                exponentials of a block are computed into registers before
-//                waiting for the previous block's PV of the half. A half
-//                moves its reference max only when the block maximum exceeds
-//                it by more than 2^8 (and then rescales O_h and l): P stays
-//                <= 256, exact in fp16, and O / l is the reference's softmax
-//                (acc * alpha + dot(P, V), kernels/prefill_attention.py:
-//                157-184) up to rounding. Warps whose 32 rows are all padding
-//                (short chunks, decode rows) do nothing; barrier arrival
-//                counts only cover the working warps.
+//                S_x(j) = Q_x K_j^T as soon as K_j is in and tile x's softmax
+//                has read S_x(j-1); O_x += P_x(j) V_j as soon as tile x
+//                published P_x(j). S_x(j+1) is computed while the softmax of
+//                tile x still works on block j, and neither tile waits behind
+//                the other.
+//   warps 2-3    idle: warpgroup 0 hands most of its registers to the softmax
+//                warpgroups (setmaxnreg).
+//   warps 4-7    softmax of tile A, warps 8-11 of tile B, one thread per row
+//                (warp w owns TMEM lanes [32 (w % 4), +32)). Per block: the
+//                row maximum first, then the exponentials into registers;
+//                only then the wait for the previous P V (which must have
+//                consumed P and updated O). The reference max moves only
+//                when the block maximum exceeds it by more than 2^8 (then O
+//                and l are rescaled): P stays <= 256, exact in fp16, and O / l
+//                is the reference's softmax (acc * alpha + dot(P, V),
+//                kernels/prefill_attention.py:157-184) up to rounding. Warps
+//                whose 32 rows are all padding (short chunks, decode rows) do
+//                nothing; barrier arrival counts cover the working warps only.
 // CTAs run most-expensive first: blockIdx.y walks the tile pairs from the
 // last (most keys) to the first.
 // All waits are bounded; on a timeout the kernel records
@@ -62,40 +65,39 @@ constexpr int kPairTokens = 2 * kTileTokens;
 constexpr int kRows = kTileTokens * kGroup;  // 126 useful rows of M = 128
 constexpr int kM = 128;
 constexpr int kBlockKeys = 128;
-constexpr int kHalfKeys = kBlockKeys / 2;
 constexpr int kPagesPerBlock = kBlockKeys / kPage;  // 8
-constexpr int kStages = 3;
+constexpr int kStages = 5;
 constexpr int kMinBlocksPerSplit = 2;
 constexpr int kMaxSplits = 16;
-constexpr int kTileThreads = 256;                   // softmax threads per tile
-constexpr int kThreads = 64 + 2 * kTileThreads;
+constexpr int kTileThreads = 128;                   // softmax threads per tile, one per row
+constexpr int kThreads = 128 + 2 * kTileThreads;    // warpgroup 0 + one per tile
+// Register split after launch (launch: 384 x 168): warpgroup 0 drops to 56,
+// the softmax warpgroups rise to 224 (128 x 56 + 256 x 224 = 384 x 168).
+constexpr uint32_t kCtrlRegs = 56;
+constexpr uint32_t kSoftmaxRegs = 224;
 constexpr float kRescaleLog2 = 8.f;                 // move the max when it grows by > 2^8
 
 constexpr int kQBytes = kM * kD * 2;               // 16 KiB
 constexpr int kQLoadBytes = kRows * kD * 2;        // 16128 bytes delivered by one box
 constexpr int kKVTileBytes = kBlockKeys * kD * 2;  // 16 KiB per K or V block
 constexpr int kStageBytes = 2 * kKVTileBytes;
-constexpr int kPBytes = kM * kBlockKeys * 2;       // 32 KiB
 constexpr int kPageBoxBytes = kPage * kD * 2;      // 2 KiB
 
 constexpr int kOffQ = 0;                                   // Q_A, Q_B
 constexpr int kOffKV = kOffQ + 2 * kQBytes;
-constexpr int kOffP = kOffKV + kStages * kStageBytes;      // P_A, P_B
-constexpr int kOffRed = kOffP + 2 * kPBytes;               // [tile][half][row] x (m, l)
-constexpr int kRedBytes = 2 * 2 * kM * 8;
-constexpr int kOffBar = kOffRed + kRedBytes;
-// barriers: kv_full[3], kv_empty[3], q_full, mma_done, then per tile:
-// s_full, s_free, p_full[2 halves], pv_done[2 halves], red_ready
-constexpr int kTileBars = 7;
+constexpr int kOffBar = kOffKV + kStages * kStageBytes;
+// barriers: kv_full[5], kv_empty[5], q_full, mma_done, then per tile:
+// s_full, s_free, p_full, pv_done
+constexpr int kTileBars = 4;
 constexpr int kNumBars = 2 * kStages + 2 + 2 * kTileBars;
 constexpr int kOffTmemPtr = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = 1024 + kOffTmemPtr + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 constexpr uint32_t kTmemCols = 512;
-// per tile x: S at 256x (128 columns), O of key half h at 256x + 128 + 64h
 constexpr uint32_t kColS = 0;
-constexpr uint32_t kColO = 128;
+constexpr uint32_t kColP = 128;
+constexpr uint32_t kColO = 192;
 
 constexpr uint32_t kIdescS = idesc_f16_f32(kM, kBlockKeys, false);
 constexpr uint32_t kIdescPV = idesc_f16_f32(kM, kD, true);
@@ -117,6 +119,8 @@ struct Params {
   int num_splits;
 };
 
+// partial record: unnormalised O[64], m (log2 units: max of score * scale *
+// log2(e)), l
 constexpr int kPartFloats = kD + 2;
 
 struct Bars {
@@ -130,12 +134,11 @@ struct Bars {
   }
   __device__ uint32_t s_full(int x) const { return tile(x, 0); }
   __device__ uint32_t s_free(int x) const { return tile(x, 1); }
-  __device__ uint32_t p_full(int x, int h) const { return tile(x, 2 + h); }
-  __device__ uint32_t pv_done(int x, int h) const { return tile(x, 4 + h); }
-  __device__ uint32_t red_ready(int x) const { return tile(x, 6); }
+  __device__ uint32_t p_full(int x) const { return tile(x, 2); }
+  __device__ uint32_t pv_done(int x) const { return tile(x, 3); }
 };
 
-// 32 lanes x 16 consecutive 32-bit TMEM columns (load and store).
+// 32 lanes x N consecutive 32-bit TMEM columns (load and store).
 __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -154,8 +157,40 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       "r"(r[15])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
 __device__ __forceinline__ void tc_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16. A row i lives in TMEM lane
+// i, two consecutive K elements per 32-bit column (lower K in the low half).
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// three-input maximum (one instruction on sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // ---- the work decomposition, shared with the merge kernel -------------------
@@ -217,8 +252,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sQ = sbase + kOffQ;
   const uint32_t sKV = sbase + kOffKV;
-  const uint32_t sP = sbase + kOffP;
-  float2* red = reinterpret_cast<float2*>(smem + kOffRed);
   const Bars bars{sbase + kOffBar};
   uint32_t* tmem_ptr_smem = reinterpret_cast<uint32_t*>(smem + kOffTmemPtr);
 
@@ -239,12 +272,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_valid_pages = (n_keys + kPage - 1) / kPage;
   const bool direct = pi.n_active == 1;                     // write O, no partial
   const int n_tiles = pi.pair_tokens > kTileTokens ? 2 : 1;
-  // rows of tile x that hold a real token: [0, 7 * tokens); quadrants that cover any
-  int n_quads[2];
-  for (int x = 0; x < 2; ++x) {
+  // lane quadrants of tile x whose rows [0, 7 * tokens) hold any real token
+  auto quads_of = [&](int x) {
     const int tt = x < n_tiles ? min(pi.pair_tokens - x * kTileTokens, kTileTokens) : 0;
-    n_quads[x] = (tt * kGroup + 31) / 32;
-  }
+    return (tt * kGroup + 31) / 32;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -254,14 +286,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bars.q_full(), 1);
     mbar_init(bars.mma_done(), 1);
     for (int x = 0; x < 2; ++x) {
-      const uint32_t quad_threads = 32u * static_cast<uint32_t>(max(n_quads[x], 1));
+      const uint32_t quad_threads = 32u * static_cast<uint32_t>(max(quads_of(x), 1));
       mbar_init(bars.s_full(x), 1);
-      mbar_init(bars.s_free(x), 2 * quad_threads);
-      mbar_init(bars.p_full(x, 0), quad_threads);
-      mbar_init(bars.p_full(x, 1), quad_threads);
-      mbar_init(bars.pv_done(x, 0), 1);
-      mbar_init(bars.pv_done(x, 1), 1);
-      mbar_init(bars.red_ready(x), 2 * quad_threads);
+      mbar_init(bars.s_free(x), quad_threads);
+      mbar_init(bars.p_full(x), quad_threads);
+      mbar_init(bars.pv_done(x), 1);
     }
     fence_mbar_init();
     // the merge kernel (programmatic stream serialization) may be scheduled
@@ -292,157 +321,156 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_ptr_smem;
 
-  if (warp == 0) {
-    // ============================ producer ====================================
-    int issued = 0;
-    bool ok = true;
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(bars.q_full(), n_tiles * kQLoadBytes);
-      tma_load_4d(sQ, &tm_q, bars.q_full(), 0, 0, h, static_cast<int>(start) + pi.tok0);
-      if (n_tiles == 2)
-        tma_load_4d(sQ + kQBytes, &tm_q, bars.q_full(), 0, 0, h,
-                    static_cast<int>(start) + pi.tok0 + kTileTokens);
-    }
-    const int64_t* bt_row = p.block_table + slot * p.bt_stride;
-    for (int j = 0; j < n_blocks; ++j) {
-      const int s = j % kStages;
-      const uint32_t use = static_cast<uint32_t>(j / kStages);
-      int page = 0;  // page ids of this block, read before waiting for the stage
-      if (lane < kPagesPerBlock) {
-        const int lp = (blk0 + j) * kPagesPerBlock + lane;
-        if (lp < n_valid_pages) {
-          int64_t pid = bt_row[lp];
-          if (pid < 0 || pid >= p.n_pages) {
-            raise_error(CIE_DEVERR_BAD_PAGE);
-            pid = 0;
-          }
-          page = static_cast<int>(pid);
-        }
-      }
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kCtrlRegs));
+    if (warp == 0) {
+      // ============================ producer ==================================
+      int issued = 0;
+      bool ok = true;
       if (lane == 0) {
-        if (j >= kStages && !mbar_wait(bars.kv_empty(s), (use & 1u) ^ 1u, CIE_DEVERR_WAIT_TIMEOUT))
-          ok = false;
-        if (ok) mbar_arrive_expect_tx(bars.kv_full(s), kStageBytes);
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+        mbar_arrive_expect_tx(bars.q_full(), n_tiles * kQLoadBytes);
+        tma_load_4d(sQ, &tm_q, bars.q_full(), 0, 0, h, static_cast<int>(start) + pi.tok0);
+        if (n_tiles == 2)
+          tma_load_4d(sQ + kQBytes, &tm_q, bars.q_full(), 0, 0, h,
+                      static_cast<int>(start) + pi.tok0 + kTileTokens);
       }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (!ok) break;
-      if (lane < kPagesPerBlock) {
-        const uint32_t dst = sKV + s * kStageBytes + lane * kPageBoxBytes;
-        tma_load_4d(dst, &tm_k, bars.kv_full(s), 0, 0, h, page);
-        tma_load_4d(dst + kKVTileBytes, &tm_v, bars.kv_full(s), 0, 0, h, page);
-      }
-      __syncwarp();
-      ++issued;
-    }
-    if (lane == 0) {
-      mbar_wait(bars.q_full(), 0, CIE_DEVERR_WAIT_TIMEOUT);
-      for (int j = max(0, issued - kStages); j < issued; ++j)
-        mbar_wait(bars.kv_full(j % kStages), static_cast<uint32_t>(j / kStages) & 1u,
-                  CIE_DEVERR_WAIT_TIMEOUT);
-    }
-  } else if (warp == 1) {
-    // ============================ MMA issuer ==================================
-    if (lane == 0) {
-      bool ok = mbar_wait(bars.q_full(), 0, CIE_DEVERR_WAIT_TIMEOUT);
-      auto wait = [&](uint32_t bar, uint32_t parity) {
-        if (ok && !mbar_wait(bar, parity, CIE_DEVERR_WAIT_TIMEOUT)) ok = false;
-        return ok;
-      };
-      auto issue_s = [&](int x, int j) {  // S_x(j) = Q_x K_j^T
-        const uint32_t k_tile = sKV + (j % kStages) * kStageBytes;
-#pragma unroll
-        for (int k = 0; k < kD / 16; ++k) {
-          const uint64_t da = smem_desc(sQ + x * kQBytes + k * 32, 16, 1024);
-          const uint64_t db = smem_desc(k_tile + k * 32, 16, 1024);
-          tc_mma_f16(tmem + x * 256 + kColS, da, db, kIdescS, k > 0 ? 1u : 0u);
-        }
-        tc_commit(bars.s_full(x));
-      };
-      auto issue_pv = [&](int x, int hh, int j) {  // O_{x,hh} (+)= P_x[:, hh] V_j[hh, :]
-        const uint32_t v_tile = sKV + (j % kStages) * kStageBytes + kKVTileBytes + hh * 8192;
-        const uint32_t p_tile = sP + x * kPBytes + hh * (kM * 128);
-#pragma unroll
-        for (int kk = 0; kk < kHalfKeys / 16; ++kk) {
-          const uint64_t da = smem_desc(p_tile + kk * 32, 16, 1024);
-          const uint64_t db = smem_desc(v_tile + kk * 2048, kKVTileBytes, 1024);
-          tc_mma_f16(tmem + x * 256 + kColO + hh * kD, da, db, kIdescPV,
-                     (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(bars.pv_done(x, hh));
-      };
-      // Event-driven issue: S_x(j) once K_j is in and tile x has read S_x(j-1);
-      // PV_{x,h}(j) once that half published P_x(j); stage j is released when
-      // every PV of block j is issued. Nothing waits behind an unrelated tile or
-      // half. test_wait never blocks; an idle poll naps briefly so the softmax
-      // warps sharing this SM sub-partition keep their issue slots.
-      int ns[2] = {0, 0};
-      int npv[2][2] = {{0, 0}, {0, 0}};
-      int released = 0;
-      const int n_halves = 2 * n_tiles;
-      int pv_left = n_blocks * n_halves;
-      unsigned long long idle_since = 0;
-      while (ok && (pv_left > 0 || released < n_blocks)) {
-        bool progress = false;
-        for (int x = 0; x < n_tiles; ++x) {
-          const int j = ns[x];
-          if (j < n_blocks &&
-              mbar_test(bars.kv_full(j % kStages), static_cast<uint32_t>(j / kStages) & 1u) &&
-              (j == 0 || mbar_test(bars.s_free(x), static_cast<uint32_t>(j - 1) & 1u))) {
-            tc_fence_after();
-            issue_s(x, j);
-            ns[x] = j + 1;
-            progress = true;
+      const int64_t* bt_row = p.block_table + slot * p.bt_stride;
+      for (int j = 0; j < n_blocks; ++j) {
+        const int s = j % kStages;
+        const uint32_t use = static_cast<uint32_t>(j / kStages);
+        int page = 0;  // page ids of this block, read before waiting for the stage
+        if (lane < kPagesPerBlock) {
+          const int lp = (blk0 + j) * kPagesPerBlock + lane;
+          if (lp < n_valid_pages) {
+            int64_t pid = bt_row[lp];
+            if (pid < 0 || pid >= p.n_pages) {
+              raise_error(CIE_DEVERR_BAD_PAGE);
+              pid = 0;
+            }
+            page = static_cast<int>(pid);
           }
         }
-        for (int x = 0; x < n_tiles; ++x) {
-          for (int hh = 0; hh < 2; ++hh) {
-            const int j = npv[x][hh];
-            if (j < ns[x] && mbar_test(bars.p_full(x, hh), static_cast<uint32_t>(j) & 1u)) {
+        if (lane == 0) {
+          if (j >= kStages &&
+              !mbar_wait(bars.kv_empty(s), (use & 1u) ^ 1u, CIE_DEVERR_WAIT_TIMEOUT))
+            ok = false;
+          if (ok) mbar_arrive_expect_tx(bars.kv_full(s), kStageBytes);
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+        if (lane < kPagesPerBlock) {
+          const uint32_t dst = sKV + s * kStageBytes + lane * kPageBoxBytes;
+          tma_load_4d(dst, &tm_k, bars.kv_full(s), 0, 0, h, page);
+          tma_load_4d(dst + kKVTileBytes, &tm_v, bars.kv_full(s), 0, 0, h, page);
+        }
+        __syncwarp();
+        ++issued;
+      }
+      // never leave the CTA with copies in flight
+      if (lane == 0) {
+        mbar_wait(bars.q_full(), 0, CIE_DEVERR_WAIT_TIMEOUT);
+        for (int j = max(0, issued - kStages); j < issued; ++j)
+          mbar_wait(bars.kv_full(j % kStages), static_cast<uint32_t>(j / kStages) & 1u,
+                    CIE_DEVERR_WAIT_TIMEOUT);
+      }
+    } else if (warp == 1) {
+      // ============================ MMA issuer ================================
+      if (lane == 0) {
+        bool ok = mbar_wait(bars.q_full(), 0, CIE_DEVERR_WAIT_TIMEOUT);
+        auto issue_s = [&](int x, int j) {  // S_x(j) = Q_x K_j^T
+          const uint32_t k_tile = sKV + (j % kStages) * kStageBytes;
+#pragma unroll
+          for (int k = 0; k < kD / 16; ++k) {
+            const uint64_t da = smem_desc(sQ + x * kQBytes + k * 32, 16, 1024);
+            const uint64_t db = smem_desc(k_tile + k * 32, 16, 1024);
+            tc_mma_f16(tmem + x * 256 + kColS, da, db, kIdescS, k > 0 ? 1u : 0u);
+          }
+          tc_commit(bars.s_full(x));
+        };
+        auto issue_pv = [&](int x, int j) {  // O_x (+)= P_x(j) V_j, P from TMEM
+          const uint32_t v_tile = sKV + (j % kStages) * kStageBytes + kKVTileBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBlockKeys / 16; ++kk) {
+            // 16 keys = 8 P columns; V: 16 keys = two 8-row swizzle atoms of 1 KiB
+            const uint64_t db = smem_desc(v_tile + kk * 2048, kKVTileBytes, 1024);
+            tc_mma_f16_ts(tmem + x * 256 + kColO, tmem + x * 256 + kColP + kk * 8, db, kIdescPV,
+                          (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(bars.pv_done(x));
+        };
+        // Event-driven issue: S_x(j) once K_j is in and tile x has read
+        // S_x(j-1); PV_x(j) once tile x published P_x(j); stage j is released
+        // when both tiles' PV(j) are issued. test_wait never blocks; an idle
+        // poll naps briefly so the softmax warps sharing this SM
+        // sub-partition keep their issue slots.
+        int ns[2] = {0, 0};
+        int npv[2] = {0, 0};
+        int released = 0;
+        int pv_left = n_blocks * n_tiles;
+        unsigned long long idle_since = 0;
+        while (ok && (pv_left > 0 || released < n_blocks)) {
+          bool progress = false;
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            if (x >= n_tiles) break;
+            const int j = ns[x];
+            if (j < n_blocks &&
+                mbar_test(bars.kv_full(j % kStages), static_cast<uint32_t>(j / kStages) & 1u) &&
+                (j == 0 || mbar_test(bars.s_free(x), static_cast<uint32_t>(j - 1) & 1u))) {
               tc_fence_after();
-              issue_pv(x, hh, j);
-              npv[x][hh] = j + 1;
+              issue_s(x, j);
+              ns[x] = j + 1;
+              progress = true;
+            }
+          }
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            if (x >= n_tiles) break;
+            const int j = npv[x];
+            if (j < ns[x] && mbar_test(bars.p_full(x), static_cast<uint32_t>(j) & 1u)) {
+              tc_fence_after();
+              issue_pv(x, j);
+              npv[x] = j + 1;
               --pv_left;
               progress = true;
             }
           }
-        }
-        while (released < n_blocks) {
-          bool all = true;
-          for (int x = 0; x < n_tiles; ++x) all = all && npv[x][0] > released && npv[x][1] > released;
-          if (!all) break;
-          tc_commit(bars.kv_empty(released % kStages));
-          ++released;
-          progress = true;
-        }
-        if (progress) {
-          idle_since = 0;
-        } else {
-          const unsigned long long now = global_timer_ns();
-          if (idle_since == 0) idle_since = now;
-          else if (now - idle_since > kWaitLimitNs) {
-            raise_error(CIE_DEVERR_WAIT_TIMEOUT);
-            ok = false;
+          while (released < n_blocks) {
+            const bool all = npv[0] > released && (n_tiles == 1 || npv[1] > released);
+            if (!all) break;
+            tc_commit(bars.kv_empty(released % kStages));
+            ++released;
+            progress = true;
           }
-          __nanosleep(32);
+          if (progress) {
+            idle_since = 0;
+          } else {
+            const unsigned long long now = global_timer_ns();
+            if (idle_since == 0) idle_since = now;
+            else if (now - idle_since > kWaitLimitNs) {
+              raise_error(CIE_DEVERR_WAIT_TIMEOUT);
+              ok = false;
+            }
+            __nanosleep(32);
+          }
         }
+        // drain: every MMA this thread issued has completed before TMEM is freed
+        tc_commit(bars.mma_done());
+        mbar_wait(bars.mma_done(), 0, CIE_DEVERR_WAIT_TIMEOUT);
       }
-      (void)wait;
-      // drain: every MMA this thread issued has completed before TMEM is freed
-      tc_commit(bars.mma_done());
-      mbar_wait(bars.mma_done(), 0, CIE_DEVERR_WAIT_TIMEOUT);
+      __syncwarp();
     }
-    __syncwarp();
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     // ============================ softmax =====================================
-    const int sw = warp - 2;                // 0..15
-    const int x = sw >> 3;                  // tile
-    const int half = (sw >> 2) & 1;         // key columns [64*half, 64*half + 64)
+    const int x = (warp >> 2) - 1;          // tile
     const int quad = warp & 3;              // TMEM lane quadrant of this warp
     const int row = quad * 32 + lane;       // tile row == TMEM lane
-    if (x < n_tiles && quad < n_quads[x]) {
+    const int n_quads = quads_of(x);
+    if (quad < n_quads) {
       const int tile_tok0 = pi.tok0 + x * kTileTokens;
       const int tile_tokens = min(pi.L - tile_tok0, kTileTokens);
       const int tok_in_tile = row / kGroup;
@@ -452,13 +480,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // use the tile's first row limit so that every value stays finite
       const int limit = pi.kv_len + tile_tok0 + (row_valid ? tok_in_tile : 0);
       const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-      const uint32_t t_s = tmem + lane_addr + x * 256 + kColS + half * kHalfKeys;
-      const uint32_t t_o = tmem + lane_addr + x * 256 + kColO + half * kD;
-      const uint32_t p_tile = sP + x * kPBytes + half * (kM * 128);
-      constexpr float kScale = 0.125f;  // head_dim ** -0.5 for D = 64
-      const float2 c2 = make_float2(kScale * kLog2e, kScale * kLog2e);
+      const uint32_t t_s = tmem + lane_addr + x * 256 + kColS;
+      const uint32_t t_p = tmem + lane_addr + x * 256 + kColP;
+      const uint32_t t_o = tmem + lane_addr + x * 256 + kColO;
+      // scores in log2 units: u = (q . k) * head_dim^-0.5 * log2(e)
+      constexpr float kC = 0.125f * kLog2e;
+      const float2 c2 = make_float2(kC, kC);
 
-      float m_ref = -CUDART_INF_F;  // scaled max the P values of this half are taken against
+      float m_ref = -CUDART_INF_F;  // log2-unit max the P values are taken against
       float l_run = 0.f;
       bool ok = true;
       for (int j = 0; j < n_blocks; ++j) {
@@ -468,48 +497,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        uint32_t sr[kHalfKeys];
-        tmem_ld_32x32b_x32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        tmem_ld_32x32b_x32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        uint32_t sr[kBlockKeys];
+#pragma unroll
+        for (int c = 0; c < kBlockKeys; c += 32)
+          tmem_ld_32x32b_x32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&sr[c]));
         tc_wait_ld();
         tc_fence_before();
         mbar_arrive(bars.s_free(x));
 
-        // raw max over my 64 columns of this block; masked columns become -inf
-        const int lim = limit - (blk0 + j) * kBlockKeys - half * kHalfKeys;
-        float mx8[8];
+        // raw row maximum of this block; masked columns become -inf
+        const int lim = limit - (blk0 + j) * kBlockKeys;
+        if (lim < kBlockKeys - 1) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) mx8[e] = -CUDART_INF_F;
-        if (lim >= kHalfKeys - 1) {
-#pragma unroll
-          for (int c = 0; c < kHalfKeys; ++c)
-            mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sr[c]));
-        } else {
-#pragma unroll
-          for (int c = 0; c < kHalfKeys; ++c) {
-            const float v = c <= lim ? __uint_as_float(sr[c]) : -CUDART_INF_F;
-            sr[c] = __float_as_uint(v);
-            mx8[c & 7] = fmaxf(mx8[c & 7], v);
-          }
+          for (int c = 0; c < kBlockKeys; ++c)
+            if (c > lim) sr[c] = __float_as_uint(-CUDART_INF_F);
         }
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
-                         kScale;
+        float mx4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          mx4[e] = fmax3(__uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1]),
+                         -CUDART_INF_F);
+#pragma unroll
+        for (int c = 8; c < kBlockKeys; c += 8)
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            mx4[e] = fmax3(mx4[e], __uint_as_float(sr[c + 2 * e]),
+                           __uint_as_float(sr[c + 2 * e + 1]));
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * kC;
 
-        // Move the reference max only when this block's max exceeds it by more
-        // than 2^8 (then l and O_h are rescaled by alpha). The exponentials go
-        // to registers first; the wait for PV(j-1) of this half, which must
-        // have consumed P(j-1) and updated O_h, comes only before P and O move.
-        const bool need = mx > m_ref + kRescaleLog2 / kLog2e;
-        const float alpha = (need && j > 0) ? ex2((m_ref - mx) * kLog2e) : 1.f;
+        const bool need = mx > m_ref + kRescaleLog2;
+        const float alpha = (need && m_ref != -CUDART_INF_F) ? ex2(m_ref - mx) : 1.f;
         if (need) m_ref = mx;
-        // no visible key in this half yet: every column is -inf and p = 0
-        const float mneg = m_ref == -CUDART_INF_F ? 0.f : -m_ref * kLog2e;
+        // no visible key yet: every column is -inf and p = 0
+        const float mneg = m_ref == -CUDART_INF_F ? 0.f : -m_ref;
         const float2 mneg2 = make_float2(mneg, mneg);
         float2 lsum0 = make_float2(0.f, 0.f), lsum1 = make_float2(0.f, 0.f);
-        uint32_t pw[kHalfKeys / 2];
+        uint32_t pw[kBlockKeys / 2];
 #pragma unroll
-        for (int c8 = 0; c8 < kHalfKeys / 8; ++c8) {
+        for (int c8 = 0; c8 < kBlockKeys / 8; ++c8) {
           float pv[8];
 #pragma unroll
           for (int e = 0; e < 8; e += 2) {
@@ -528,16 +553,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         l_run = l_run * alpha + ((lsum0.x + lsum0.y) + (lsum1.x + lsum1.y));
 
-        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(bars.pv_done(x, half), par ^ 1u,
+        // PV(j-1) must have consumed P(j-1) and finished updating O
+        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(bars.pv_done(x), par ^ 1u,
                                                          CIE_DEVERR_WAIT_TIMEOUT))) {
           ok = false;
           break;
         }
-        // TMEM round trip of O_h by the whole warp when any of its rows moved
-        // its max; the other rows multiply by 1. O_h holds nothing before the
+        tc_fence_after();
+        // TMEM round trip of O by the whole warp when any of its rows moved
+        // its max; the other rows multiply by 1. O holds nothing before the
         // first PV of this CTA (j == 0).
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
-          tc_fence_after();
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
           for (int c = 0; c < kD; c += 16) {  // 16 columns at a time: few live registers
             uint32_t o[16];
@@ -547,95 +573,71 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int d = 0; d < 16; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
             tmem_st_32x32b_x16(t_o + c, o);
           }
-          tc_wait_st();
-          tc_fence_before();
         }
-#pragma unroll
-        for (int c8 = 0; c8 < kHalfKeys / 8; ++c8) {
-          // K-major, 128B swizzle: keys [64*half, 64*half+64) form atom column `half`
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(p_tile + sw128(row, c8)),
-                       "r"(pw[c8 * 4 + 0]), "r"(pw[c8 * 4 + 1]), "r"(pw[c8 * 4 + 2]),
-                       "r"(pw[c8 * 4 + 3])
-                       : "memory");
-        }
+        tmem_st_32x32b_x32(t_p, pw);
+        tmem_st_32x32b_x32(t_p + 32, pw + 32);
 
         // V rows past the pair's last key hold stale pool data: zero them so
-        // that 0 * (non-finite) cannot reach an accumulator. The working
-        // threads of (tile x, key half h) zero the stale rows among V rows
-        // [64h, 64h + 64) before their p_full arrival below, so PV(x, h) reads
-        // zeros; both tiles do it (the same zeros) because their PVs are
-        // issued independently.
+        // that 0 * (non-finite) cannot reach an accumulator. Each tile's
+        // working threads write the (same) zeros before their own p_full
+        // arrival, because the two tiles' PVs are issued independently.
         if (blk0 + j == pi.n_blocks - 1) {
-          const int first = max(n_keys - (blk0 + j) * kBlockKeys, half * kHalfKeys);
-          const int rows = (half + 1) * kHalfKeys - first;
+          const int first = n_keys - (blk0 + j) * kBlockKeys;
+          const int rows = kBlockKeys - first;
           if (rows > 0) {
             const uint32_t vtile = sKV + (j % kStages) * kStageBytes + kKVTileBytes;
-            const int nthr = 32 * n_quads[x];
+            const int nthr = 32 * n_quads;
             for (int e = quad * 32 + lane; e < rows * 8; e += nthr) {
               asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(
                                vtile + sw128(first + (e >> 3), e & 7)),
                            "r"(0)
                            : "memory");
             }
+            fence_proxy_async_smem();
           }
         }
-        fence_proxy_async_smem();
-        mbar_arrive(bars.p_full(x, half));
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(bars.p_full(x));
       }
-      // last PV of this half, then combine the two halves of the row
+      // last PV of this tile
       if (ok && n_blocks > 0)
-        ok = __all_sync(0xffffffffu, mbar_wait(bars.pv_done(x, half),
+        ok = __all_sync(0xffffffffu, mbar_wait(bars.pv_done(x),
                                                static_cast<uint32_t>(n_blocks - 1) & 1u,
                                                CIE_DEVERR_WAIT_TIMEOUT));
-      red[(x * 2 + half) * kM + row] = make_float2(m_ref, l_run);
-      mbar_arrive(bars.red_ready(x));
-      mbar_wait(bars.red_ready(x), 0, CIE_DEVERR_WAIT_TIMEOUT);
-      const float2 a = red[(x * 2 + 0) * kM + row];
-      const float2 c = red[(x * 2 + 1) * kM + row];
-      const float M = fmaxf(a.x, c.x);
-      const float w0 = a.x == -CUDART_INF_F ? 0.f : ex2((a.x - M) * kLog2e);
-      const float w1 = c.x == -CUDART_INF_F ? 0.f : ex2((c.x - M) * kLog2e);
-      const float l_tot = a.y * w0 + c.y * w1;
-      // this thread produces output columns [32*half, 32*half + 32) of its row
       tc_fence_after();
-      float out[32];
-#pragma unroll
-      for (int c16 = 0; c16 < 2; ++c16) {
-        uint32_t o0[16], o1[16];
-        const uint32_t col = half * 32 + c16 * 16;
-        tmem_ld_32x32b_x16(tmem + lane_addr + x * 256 + kColO + col, o0);
-        tmem_ld_32x32b_x16(tmem + lane_addr + x * 256 + kColO + kD + col, o1);
-        tc_wait_ld();
-#pragma unroll
-        for (int d = 0; d < 16; ++d)
-          out[c16 * 16 + d] = __uint_as_float(o0[d]) * w0 + __uint_as_float(o1[d]) * w1;
-      }
+      uint32_t ob[kD];
+      tmem_ld_32x32b_x32(t_o, *reinterpret_cast<uint32_t(*)[32]>(&ob[0]));
+      tmem_ld_32x32b_x32(t_o + 32, *reinterpret_cast<uint32_t(*)[32]>(&ob[32]));
+      tc_wait_ld();
       if (ok && row_valid) {
         const int64_t tok = start + tile_tok0 + tok_in_tile;
         const int hq = h * kGroup + head_in_group;
         if (direct) {
-          const float inv = 1.f / l_tot;
-          __half* dst = p.o + (tok * p.num_q_heads + hq) * kD + half * 32;
+          const float inv = 1.f / l_run;
+          __half* dst = p.o + (tok * p.num_q_heads + hq) * kD;
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
+          for (int cc = 0; cc < kD / 8; ++cc) {
             uint4 w;
-            w.x = pack_half2(out[cc * 8 + 0] * inv, out[cc * 8 + 1] * inv);
-            w.y = pack_half2(out[cc * 8 + 2] * inv, out[cc * 8 + 3] * inv);
-            w.z = pack_half2(out[cc * 8 + 4] * inv, out[cc * 8 + 5] * inv);
-            w.w = pack_half2(out[cc * 8 + 6] * inv, out[cc * 8 + 7] * inv);
+            w.x = pack_half2(__uint_as_float(ob[cc * 8 + 0]) * inv,
+                             __uint_as_float(ob[cc * 8 + 1]) * inv);
+            w.y = pack_half2(__uint_as_float(ob[cc * 8 + 2]) * inv,
+                             __uint_as_float(ob[cc * 8 + 3]) * inv);
+            w.z = pack_half2(__uint_as_float(ob[cc * 8 + 4]) * inv,
+                             __uint_as_float(ob[cc * 8 + 5]) * inv);
+            w.w = pack_half2(__uint_as_float(ob[cc * 8 + 6]) * inv,
+                             __uint_as_float(ob[cc * 8 + 7]) * inv);
             reinterpret_cast<uint4*>(dst)[cc] = w;
           }
         } else {
           float* rec = p.part + ((static_cast<int64_t>(split) * p.total_tokens + tok) *
                                      p.num_q_heads + hq) * kPartFloats;
 #pragma unroll
-          for (int cc = 0; cc < 16; ++cc)
-            reinterpret_cast<float2*>(rec + half * 32)[cc] =
-                make_float2(out[cc * 2 + 0], out[cc * 2 + 1]);
-          if (half == 0) {
-            rec[kD] = M;  // -inf when this key range had no visible key for the row
-            rec[kD + 1] = l_tot;
-          }
+          for (int cc = 0; cc < kD / 2; ++cc)
+            reinterpret_cast<float2*>(rec)[cc] =
+                make_float2(__uint_as_float(ob[cc * 2 + 0]), __uint_as_float(ob[cc * 2 + 1]));
+          rec[kD] = m_ref;  // -inf when this key range had no visible key for the row
+          rec[kD + 1] = l_run;
         }
       }
     }
@@ -648,10 +650,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Combines the key-range partials of the tile pairs that were split: per row,
-// O = sum_s w_s acc_s / sum_s w_s l_s with w_s = exp(m_s - max m). One warp per
-// row (blockIdx.z picks 8 rows of the pair): lane s < splits loads (m_s, l_s)
-// so the maximum and the denominator are warp reductions, then every lane
-// accumulates two output columns over the splits. Launched with programmatic
+// O = sum_s w_s acc_s / sum_s w_s l_s with w_s = 2^(m_s - max m), m in log2
+// units. One warp per row (blockIdx.z picks 8 rows of the pair): lane
+// s < splits loads (m_s, l_s) so the maximum and the denominator are warp
+// reductions, then every lane accumulates two output columns over the splits. Launched with programmatic
 // stream serialization: griddepcontrol.wait holds it until the attention
 // kernel has finished and its writes are visible.
 __global__ void __launch_bounds__(256) mixed_merge_kernel(const Params p) {
@@ -676,7 +678,7 @@ __global__ void __launch_bounds__(256) mixed_merge_kernel(const Params p) {
   float M = m;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  const float w = (lane < pi.n_active && m != -CUDART_INF_F) ? ex2((m - M) * kLog2e) : 0.f;
+  const float w = (lane < pi.n_active && m != -CUDART_INF_F) ? ex2(m - M) : 0.f;
   float den = w * l;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
