@@ -62,6 +62,10 @@ def parse_args(argv=None):
                     help="bound on the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-mixed", action="store_true", help="skip the mixed-attention lines")
+    ap.add_argument("--no-serving", action="store_true",
+                    help="skip the Qwen2.5-0.5B-shape model line (serving tok/s)")
+    ap.add_argument("--serve-batch", type=int, default=64, help="sequences per GPU")
+    ap.add_argument("--serve-steps", type=int, default=128, help="timed decode steps")
     ap.add_argument("--sweep", action="store_true",
                     help="print one JSON line per decode sweep point (configs 2 and 5) "
                          "instead of the benchmark line")
@@ -400,6 +404,77 @@ def run_sweep(args, dev):
         torch.cuda.empty_cache()
 
 
+def serving_line(args, rank, world, dev):
+    """Qwen2.5-0.5B-shape model through the paged ops (every rank its own replica).
+
+    Random-init model (HF initialiser, N(0, 0.02), seed 0, fp16). Per GPU,
+    ``serve_batch`` prompts of uniform random ids with lognormal lengths (median
+    512, sigma 0.5, capped at 4096; seed 1000 + rank) are prefilled through the
+    mixed op in passes of at most 2048 tokens, then ``serve_steps`` greedy decode
+    steps run as one CUDA graph each (embedding, 24 layers with the paged decode
+    op and the KV scatter, lm_head, argmax). Decode tok/s = sequences x steps of
+    all ranks / max-over-ranks device time; the last step's tokens are read back
+    to the host."""
+    import numpy as np
+    from custom_inference_engine_b200 import model_runner as MR
+
+    B, K = args.serve_batch, args.serve_steps
+    cfg = MR.qwen2_config()
+    model = MR.random_qwen2(cfg, seed=0, device=dev)
+    rng = np.random.default_rng(1000 + rank)
+    plens = np.clip(np.round(np.exp(rng.normal(np.log(512.0), 0.5, size=B))), 1, 4096).astype(int)
+    prompts = [rng.integers(0, cfg.vocab_size, size=int(n)).tolist() for n in plens]
+    warm = 3
+    cap = [int(n) + warm + K + 1 for n in plens]
+    runner = MR.PagedRunner(model, max_cache_len=sum(c + MR.PAGE_SIZE for c in cap),
+                            n_slots=B + 1, token_budget=2048)
+    slots = list(range(1, B + 1))
+    for s, c in zip(slots, cap):
+        runner.admit(s, c)
+    stream = torch.cuda.current_stream()
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    p0 = torch.cuda.Event(enable_timing=True)
+    p1 = torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    pre = runner.prefill(slots, prompts)
+    p1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = dist_max(p0.elapsed_time(p1), world, dev)
+    graph = runner.decode_graph(slots, pre.first_tokens, capture=True)
+    for _ in range(warm):
+        graph.step()
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    d0 = torch.cuda.Event(enable_timing=True)
+    d1 = torch.cuda.Event(enable_timing=True)
+    d0.record(stream)
+    for _ in range(K):
+        graph.step()
+    d1.record(stream)
+    last = graph.tokens.cpu()
+    torch.cuda.synchronize()
+    decode_ms = dist_max(d0.elapsed_time(d1), world, dev)
+    out = {
+        "model": "Qwen2.5-0.5B shape (24 layers, hidden 896, 14q/2kv heads, D 64, MLP 4864, "
+                 "vocab 151936, tied), random init N(0, 0.02), fp16, greedy",
+        "decode_tok_s": B * K * world / (decode_ms / 1e3),
+        "decode_ms_per_step": decode_ms / K,
+        "batch_per_gpu": B, "decode_steps": K,
+        "prompt_tokens_per_gpu": int(plens.sum()),
+        "prefill_tok_s": float(plens.sum()) * world / (prefill_ms / 1e3),
+        "prefill_passes": pre.forward_passes,
+        "last_tokens_read_back": int(last.numel()),
+        "workload": "closed batch: lognormal prompts (median 512) prefilled through the mixed "
+                    "op in 2048-token passes, then CUDA-graphed greedy decode through the decode "
+                    "op; not the Poisson scheduler workload (no request queue)",
+    }
+    del graph, runner, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, rank, world, local):
     from custom_inference_engine_b200 import cabi, native
     from custom_inference_engine_b200 import workloads as W
@@ -475,6 +550,7 @@ def run_ours(args, rank, world, local):
     e2e_ms = dist_max(e0.elapsed_time(e1), world, dev)
     e2e_value = nbytes * world * e2e_steps / (e2e_ms / 1e3) / 1e9
     ok = torch.equal(out_host, step().cpu())
+    serving = None if args.no_serving else serving_line(args, rank, world, dev)
 
     result = None
     if rank == 0:
@@ -499,6 +575,8 @@ def run_ours(args, rank, world, local):
             "clocks": clocks.summary(),
             "device_error_bits": errs,
         }
+        if serving is not None:
+            result["serving"] = serving
         if not args.no_mixed:
             result["mixed"] = mixed_lines(dev)
         if not args.no_cpu_baseline and world == 1:

@@ -61,13 +61,16 @@ class KVStorage:
         _decode_update(self.keys[layer_num], self.values[layer_num], self.lens, slot_ids,
                        self.block_table, k_proj, v_proj)
 
+    # The padding slot's length is reset with an in-place fill of a one-element
+    # slice rather than ``lens[0] = 0``: the latter copies a host scalar, which a
+    # CUDA graph capture rejects.
     def decode_advance(self, slot_ids: torch.Tensor) -> None:
         self.lens[slot_ids] += 1
-        self.lens[self.unused_idx] = 0
+        self.lens[self.unused_idx:self.unused_idx + 1].zero_()
 
     def mixed_advance(self, slot_ids: torch.Tensor, lens: torch.Tensor) -> None:
         self.lens[slot_ids] += lens
-        self.lens[self.unused_idx] = 0
+        self.lens[self.unused_idx:self.unused_idx + 1].zero_()
 
     def reset(self, slot_ids) -> None:
         self.lens[slot_ids] = 0
