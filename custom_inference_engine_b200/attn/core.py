@@ -29,6 +29,8 @@ native.load_ops()
 
 gqa_decode_attention_op = torch.ops.inference.gqa_decode_attention
 gqa_mixed_attention_op = torch.ops.inference.gqa_mixed_attention
+rope_kv_decode_update_op = torch.ops.inference.rope_kv_decode_update
+rope_kv_mixed_update_op = torch.ops.inference.rope_kv_mixed_update
 _gqa_decode_attention_splits = torch.ops.inference.gqa_decode_attention_splits
 
 # The reference tunes Triton tiles here (attn/core.py:114-116). The CUDA decode
@@ -87,12 +89,16 @@ class TritonQwen2Attention(torch.nn.Module):
     """HF ``Qwen2Attention`` replacement that runs the paged CUDA attention.
 
     With ``kv_manager`` (a ``KVStorage``) and ``metadata`` (an
-    ``AttentionMetadata``) it computes the fused QKV projection, RoPE, writes
-    the new K/V rows into the pages (``decode_update`` when
-    ``metadata.full_decode`` else ``mixed_update``) and runs the matching
-    attention op, then ``o_proj``. Without ``kv_manager`` it defers to the
-    wrapped HF module.
+    ``AttentionMetadata``) it computes the fused QKV projection, then ONE launch
+    rotates q and k and writes the new K/V rows into the pages (the decode or
+    the mixed addressing of ``KVStorage.decode_update`` / ``mixed_update``,
+    bit-identical to HF's ``apply_rotary_pos_emb`` followed by those updates),
+    runs the matching attention op, then ``o_proj``. ``fuse_rope = False``
+    restores the reference's sequence (HF RoPE, then ``kv_manager``'s update
+    methods). Without ``kv_manager`` it defers to the wrapped HF module.
     """
+
+    fuse_rope = True
 
     def __init__(self, original_attn):
         super().__init__()
@@ -126,20 +132,32 @@ class TritonQwen2Attention(torch.nn.Module):
 
         total_T = hidden_states.shape[1]
         shape = (1, total_T, -1, self.head_dim)
-        q, k, v = torch.nn.functional.linear(hidden_states, self.qkv_weight,
-                                             self.qkv_bias).split(self.qkv_sizes, dim=-1)
+        qkv = torch.nn.functional.linear(hidden_states, self.qkv_weight, self.qkv_bias)
         cos, sin = position_embeddings
-        q, k = apply_rotary_pos_emb(q.view(shape), k.view(shape), cos, sin, unsqueeze_dim=2)
-        v = v.view(shape)
         layer = self.layer_idx
+        if self.fuse_rope:
+            if metadata.full_decode:
+                q = rope_kv_decode_update_op(qkv, cos, sin, kv_manager.keys[layer],
+                                             kv_manager.values[layer], kv_manager.lens,
+                                             metadata.slot_ids, kv_manager.block_table)
+            else:
+                q = rope_kv_mixed_update_op(qkv, cos, sin, kv_manager.keys[layer],
+                                            kv_manager.values[layer], metadata.pages,
+                                            metadata.offsets)
+        else:
+            q, k, v = qkv.split(self.qkv_sizes, dim=-1)
+            q, k = apply_rotary_pos_emb(q.view(shape), k.view(shape), cos, sin, unsqueeze_dim=2)
+            v = v.view(shape)
+            if metadata.full_decode:
+                kv_manager.decode_update(layer, metadata.slot_ids, k, v)
+            else:
+                kv_manager.mixed_update(layer, metadata.pages, metadata.offsets, k, v)
         if metadata.full_decode:
-            kv_manager.decode_update(layer, metadata.slot_ids, k, v)
             o = gqa_decode_attention_op(q, kv_manager.keys[layer], kv_manager.values[layer],
                                         kv_manager.lens[metadata.slot_ids] + 1,
                                         slot_ids=metadata.slot_ids,
                                         block_table=kv_manager.block_table)
         else:
-            kv_manager.mixed_update(layer, metadata.pages, metadata.offsets, k, v)
             o = gqa_mixed_attention_op(q, kv_manager.keys[layer], kv_manager.values[layer],
                                        kv_lens=kv_manager.lens[metadata.slot_ids],
                                        max_seqlen=metadata.max_seqlen,

@@ -115,3 +115,40 @@ def kv_mixed_update(k_cache, v_cache, pages, offsets, k_new, v_new, stream=None)
         k_cache.stride(0), k_cache.stride(1), k_new.stride(1), k_new.stride(2), v_new.stride(1),
         v_new.stride(2), native.stream_ptr(stream))
     native.check(st, "cie_kv_mixed_update")
+
+
+def _rope_q_out(qkv, k_cache, out):
+    d, hkv = k_cache.shape[3], k_cache.shape[1]
+    hq = qkv.shape[-1] // d - 2 * hkv
+    if out is None:
+        out = torch.empty((1, qkv.shape[1], hq, d), dtype=qkv.dtype, device=qkv.device)
+    return out, hq
+
+
+def rope_kv_decode_update(qkv, cos, sin, k_cache, v_cache, lens, slot_ids, block_table,
+                          out=None, stream=None):
+    """cie_rope_kv_decode_update: rotated q (returned) and the token's rotated k / v
+    written at its slot's current length."""
+    out, hq = _rope_q_out(qkv, k_cache, out)
+    st = native.lib().cie_rope_kv_decode_update(
+        _p(qkv), qkv.stride(1), _p(cos), _p(sin), cos.stride(1), _p(out), _p(k_cache),
+        _p(v_cache), _p(lens), _p(slot_ids), _p(block_table), slot_ids.shape[0], hq,
+        k_cache.shape[1], k_cache.shape[3], k_cache.shape[2], k_cache.shape[0],
+        min(lens.shape[0], block_table.shape[0]), block_table.stride(0), k_cache.stride(0),
+        k_cache.stride(1), native.stream_ptr(stream))
+    native.check(st, "cie_rope_kv_decode_update")
+    return out
+
+
+def rope_kv_mixed_update(qkv, cos, sin, k_cache, v_cache, pages, offsets, out=None,
+                         stream=None):
+    """cie_rope_kv_mixed_update: rotated q (returned); token t's rotated k / v to
+    (pages[t], offsets[t])."""
+    out, hq = _rope_q_out(qkv, k_cache, out)
+    st = native.lib().cie_rope_kv_mixed_update(
+        _p(qkv), qkv.stride(1), _p(cos), _p(sin), cos.stride(1), _p(out), _p(k_cache),
+        _p(v_cache), _p(pages), _p(offsets), pages.shape[0], hq, k_cache.shape[1],
+        k_cache.shape[3], k_cache.shape[2], k_cache.shape[0], k_cache.stride(0),
+        k_cache.stride(1), native.stream_ptr(stream))
+    native.check(st, "cie_rope_kv_mixed_update")
+    return out

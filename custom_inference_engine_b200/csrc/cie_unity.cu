@@ -6,3 +6,4 @@
 #include "decode_noalloc.cu"
 #include "kv_update.cu"
 #include "mixed_attention.cu"
+#include "rope_kv.cu"

@@ -191,6 +191,84 @@ void kv_mixed_update(at::Tensor& k_cache, at::Tensor& v_cache, const at::Tensor&
   check_status(st, "kv_mixed_update");
 }
 
+void check_rope_src(const at::Tensor& qkv, const at::Tensor& cos, const at::Tensor& sin,
+                    const at::Tensor& kc, const at::Tensor& vc) {
+  TORCH_CHECK(qkv.is_cuda() && cos.is_cuda() && sin.is_cuda(), "qkv / cos / sin must be CUDA");
+  TORCH_CHECK(qkv.scalar_type() == at::kHalf && cos.scalar_type() == at::kHalf &&
+                  sin.scalar_type() == at::kHalf,
+              "qkv / cos / sin must be float16");
+  TORCH_CHECK(kc.is_cuda() && vc.is_cuda() && kc.scalar_type() == at::kHalf &&
+                  vc.scalar_type() == at::kHalf,
+              "caches must be float16 CUDA tensors");
+  TORCH_CHECK(kc.dim() == 4 && kc.sizes() == vc.sizes() && kc.strides() == vc.strides() &&
+                  kc.stride(3) == 1 && kc.stride(2) == kc.size(3),
+              "k_cache / v_cache must be (n_pages, H_kv, page_size, D) with dense rows");
+  TORCH_CHECK(qkv.dim() == 3 && qkv.size(0) == 1 && qkv.stride(2) == 1,
+              "qkv must be (1, T, (H_q + 2 H_kv) * D) with unit inner stride");
+  TORCH_CHECK(qkv.size(2) % kc.size(3) == 0 && qkv.size(2) / kc.size(3) > 2 * kc.size(1),
+              "qkv width must be (H_q + 2 H_kv) * D");
+  TORCH_CHECK(cos.dim() == 3 && cos.sizes() == sin.sizes() && cos.strides() == sin.strides() &&
+                  cos.size(0) == 1 && cos.size(1) == qkv.size(1) && cos.size(2) == kc.size(3) &&
+                  cos.stride(2) == 1,
+              "cos / sin must be (1, T, D) with unit inner stride");
+}
+
+at::Tensor rope_out(const at::Tensor& qkv, const at::Tensor& kc) {
+  const int64_t d = kc.size(3);
+  const int64_t hq = qkv.size(2) / d - 2 * kc.size(1);
+  return at::empty({1, qkv.size(1), hq, d}, qkv.options());
+}
+
+at::Tensor rope_kv_decode_update(const at::Tensor& qkv, const at::Tensor& cos,
+                                 const at::Tensor& sin, at::Tensor& k_cache, at::Tensor& v_cache,
+                                 const at::Tensor& lens, const at::Tensor& slot_ids,
+                                 const at::Tensor& block_table) {
+  check_rope_src(qkv, cos, sin, k_cache, v_cache);
+  check_i64(lens, "lens");
+  check_i64(slot_ids, "slot_ids");
+  check_i64(block_table, "block_table");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.stride(1) == 1, "block_table must be 2-D");
+  TORCH_CHECK(slot_ids.dim() == 1 && slot_ids.size(0) == qkv.size(1), "one token per slot id");
+  TORCH_CHECK(lens.is_contiguous() && slot_ids.is_contiguous(), "lens / slot_ids contiguous");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  at::Tensor q = rope_out(qkv, k_cache);
+  const int st = cie_rope_kv_decode_update(
+      qkv.data_ptr(), qkv.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1),
+      q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr<int64_t>(),
+      slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(),
+      static_cast<int>(slot_ids.size(0)), static_cast<int>(q.size(2)),
+      static_cast<int>(k_cache.size(1)), static_cast<int>(k_cache.size(3)),
+      static_cast<int>(k_cache.size(2)), k_cache.size(0),
+      lens.size(0) < block_table.size(0) ? lens.size(0) : block_table.size(0),
+      block_table.stride(0), k_cache.stride(0), k_cache.stride(1),
+      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "rope_kv_decode_update");
+  return q;
+}
+
+at::Tensor rope_kv_mixed_update(const at::Tensor& qkv, const at::Tensor& cos,
+                                const at::Tensor& sin, at::Tensor& k_cache, at::Tensor& v_cache,
+                                const at::Tensor& pages, const at::Tensor& offsets) {
+  check_rope_src(qkv, cos, sin, k_cache, v_cache);
+  check_i64(pages, "pages");
+  check_i64(offsets, "offsets");
+  TORCH_CHECK(pages.dim() == 1 && offsets.dim() == 1 && pages.size(0) == offsets.size(0) &&
+                  pages.size(0) == qkv.size(1),
+              "pages / offsets must be (T,) matching qkv");
+  TORCH_CHECK(pages.is_contiguous() && offsets.is_contiguous(), "pages / offsets contiguous");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  at::Tensor q = rope_out(qkv, k_cache);
+  const int st = cie_rope_kv_mixed_update(
+      qkv.data_ptr(), qkv.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1),
+      q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), pages.data_ptr<int64_t>(),
+      offsets.data_ptr<int64_t>(), pages.size(0), static_cast<int>(q.size(2)),
+      static_cast<int>(k_cache.size(1)), static_cast<int>(k_cache.size(3)),
+      static_cast<int>(k_cache.size(2)), k_cache.size(0), k_cache.stride(0), k_cache.stride(1),
+      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "rope_kv_mixed_update");
+  return q;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(inference, m) {
@@ -209,6 +287,12 @@ TORCH_LIBRARY(inference, m) {
   m.def(
       "kv_mixed_update(Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor pages, Tensor offsets, "
       "Tensor k_new, Tensor v_new) -> ()");
+  m.def(
+      "rope_kv_decode_update(Tensor qkv, Tensor cos, Tensor sin, Tensor(a!) k_cache, "
+      "Tensor(b!) v_cache, Tensor lens, Tensor slot_ids, Tensor block_table) -> Tensor");
+  m.def(
+      "rope_kv_mixed_update(Tensor qkv, Tensor cos, Tensor sin, Tensor(a!) k_cache, "
+      "Tensor(b!) v_cache, Tensor pages, Tensor offsets) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(inference, CUDA, m) {
@@ -217,4 +301,6 @@ TORCH_LIBRARY_IMPL(inference, CUDA, m) {
   m.impl("gqa_decode_attention_splits", &gqa_decode_attention_splits);
   m.impl("kv_decode_update", &kv_decode_update);
   m.impl("kv_mixed_update", &kv_mixed_update);
+  m.impl("rope_kv_decode_update", &rope_kv_decode_update);
+  m.impl("rope_kv_mixed_update", &rope_kv_mixed_update);
 }

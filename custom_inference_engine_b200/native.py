@@ -54,6 +54,12 @@ SIGNATURES = {
     "cie_kv_mixed_update": (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_int,
                                     c_int, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                     c_i64, c_ptr]),
+    "cie_rope_kv_decode_update": (c_int, [c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr,
+                                          c_ptr, c_ptr, c_ptr, c_int, c_int, c_int, c_int, c_int,
+                                          c_i64, c_i64, c_i64, c_i64, c_i64, c_ptr]),
+    "cie_rope_kv_mixed_update": (c_int, [c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr,
+                                         c_ptr, c_ptr, c_i64, c_int, c_int, c_int, c_int, c_i64,
+                                         c_i64, c_i64, c_ptr]),
 }
 
 CIE_OK = 0
@@ -138,6 +144,19 @@ def _register_fakes() -> None:
     @torch.library.register_fake("inference::kv_mixed_update")
     def _mix_upd_fake(k_cache, v_cache, pages, offsets, k_new, v_new):
         return None
+
+    def _rope_out(qkv, k_cache):
+        hkv, d = k_cache.shape[1], k_cache.shape[3]
+        hq = qkv.shape[-1] // d - 2 * hkv
+        return qkv.new_empty((1, qkv.shape[1], hq, d))
+
+    @torch.library.register_fake("inference::rope_kv_decode_update")
+    def _rope_dec_fake(qkv, cos, sin, k_cache, v_cache, lens, slot_ids, block_table):
+        return _rope_out(qkv, k_cache)
+
+    @torch.library.register_fake("inference::rope_kv_mixed_update")
+    def _rope_mix_fake(qkv, cos, sin, k_cache, v_cache, pages, offsets):
+        return _rope_out(qkv, k_cache)
 
 
 def stream_ptr(stream=None) -> int:

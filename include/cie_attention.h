@@ -5,8 +5,8 @@
  * Every entry point takes plain device pointers, sizes and strides (in
  * elements), launches asynchronously on `stream`, performs no host<->device
  * synchronisation and allocates nothing. cie_decode_attention,
- * cie_mixed_attention, cie_kv_decode_update and cie_kv_mixed_update can be
- * captured in a CUDA graph. Return value: CIE_OK or a negative cie_status; on
+ * cie_mixed_attention, cie_kv_decode_update, cie_kv_mixed_update and the two
+ * cie_rope_kv_*_update entry points can be captured in a CUDA graph. Return value: CIE_OK or a negative cie_status; on
  * error nothing was launched and cie_last_error_message() (thread-local) says
  * why.
  *
@@ -184,6 +184,42 @@ int cie_kv_mixed_update(void* k_cache, void* v_cache, const int64_t* pages,
                         int64_t n_pages, int64_t cache_page_stride, int64_t cache_head_stride,
                         int64_t k_tok_stride, int64_t k_head_stride, int64_t v_tok_stride,
                         int64_t v_head_stride, cie_stream_t stream);
+
+/* ---- rotary embedding fused with the KV-page scatter ----------------------- */
+
+/*
+ * One launch per layer for what the reference does between the fused QKV
+ * projection and the attention op (attn/core.py:193-206): rotary embedding of
+ * q and k (transformers Qwen2 apply_rotary_pos_emb: x * cos + rotate_half(x) *
+ * sin, each operation rounded to fp16 as there, so results are bit-identical)
+ * and KVStorage.decode_update (kv_cache/storage.py:87-122).
+ *   qkv     (1, batch, (num_q_heads + 2 num_kv_heads) * head_dim) fp16, rows
+ *           qkv_tok_stride elements apart: q heads, then k heads, then v heads.
+ *   cos/sin (1, batch, head_dim) fp16, rows cs_tok_stride apart.
+ *   q_out   (1, batch, num_q_heads, head_dim) fp16 contiguous: rotated q.
+ * Rotated k and plain v of token i land where cie_kv_decode_update puts them
+ * (slot slot_ids[i] at position lens[slot]). Every row 16-byte aligned;
+ * head_dim 64.
+ */
+int cie_rope_kv_decode_update(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                              const void* sin, int64_t cs_tok_stride, void* q_out,
+                              void* k_cache, void* v_cache, const int64_t* lens,
+                              const int64_t* slot_ids, const int64_t* block_table, int batch,
+                              int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                              int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                              int64_t cache_page_stride, int64_t cache_head_stride,
+                              cie_stream_t stream);
+
+/*
+ * The same for a mixed pass (KVStorage.mixed_update, kv_cache/storage.py:62-85):
+ * token t's rotated k and v go to page pages[t], offset offsets[t].
+ */
+int cie_rope_kv_mixed_update(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                             const void* sin, int64_t cs_tok_stride, void* q_out, void* k_cache,
+                             void* v_cache, const int64_t* pages, const int64_t* offsets,
+                             int64_t num_tokens, int num_q_heads, int num_kv_heads, int head_dim,
+                             int page_size, int64_t n_pages, int64_t cache_page_stride,
+                             int64_t cache_head_stride, cie_stream_t stream);
 
 #ifdef __cplusplus
 }

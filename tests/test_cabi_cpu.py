@@ -94,5 +94,18 @@ def test_mixed_and_update_argument_checks():
     assert lib.cie_mixed_default_splits(1, 1, 2, -1) == 16
     assert lib.cie_kv_mixed_update(None, p, p, p, p, p, 4, 2, 64, 16, 10, 2048, 1024, 1152, 64,
                                    1152, 64, None) == -1
+    # fused RoPE + KV write: qkv row 1152, cos/sin row 64, pool strides 2048 / 1024
+    assert lib.cie_rope_kv_mixed_update(p, 1152, p, p, 64, p, p, p, p, p, 0, 14, 2, 64, 16, 10,
+                                        2048, 1024, None) == 0  # nothing to do
+    assert lib.cie_rope_kv_mixed_update(p, 1152, p, p, 64, p, p, p, None, p, 4, 14, 2, 64, 16,
+                                        10, 2048, 1024, None) == -1
+    assert lib.cie_rope_kv_mixed_update(p, 1152, p, p, 64, p, p, p, p, p, 4, 14, 2, 128, 16,
+                                        10, 2048, 1024, None) == -2
+    assert lib.cie_rope_kv_mixed_update(p, 1000, p, p, 64, p, p, p, p, p, 4, 14, 2, 64, 16,
+                                        10, 2048, 1024, None) == -1   # rows overlap
+    assert lib.cie_rope_kv_mixed_update(p + 2, 1152, p, p, 64, p, p, p, p, p, 4, 14, 2, 64, 16,
+                                        10, 2048, 1024, None) == -4   # misaligned
+    assert lib.cie_rope_kv_decode_update(p, 1152, p, p, 64, p, p, p, None, p, p, 4, 14, 2, 64,
+                                         16, 10, 3, 10, 2048, 1024, None) == -1
     assert lib.cie_kv_decode_update(p, p, p, p, p, p, p, 4, 2, 64, 16, 10, 3, 10, 100, 1024,
                                     1152, 64, 1152, 64, None) == -1

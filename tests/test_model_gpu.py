@@ -67,6 +67,23 @@ def test_greedy_tokens_match_hf_attention(cuda_device):
         assert ours[i] == ref[i][0], (i, ours[i], ref[i][0])
 
 
+def test_fused_rope_matches_reference_sequence(cuda_device):
+    """The fused RoPE + KV write gives the same bits as HF's RoPE followed by
+    KVStorage's updates (the module's ``fuse_rope = False`` path)."""
+    from custom_inference_engine_b200.attn import core
+
+    model = _model(cuda_device)
+    prompts = _prompts()
+    fused, pre_f = _ours(model, prompts, capture=False)
+    core.TritonQwen2Attention.fuse_rope = False
+    try:
+        plain, pre_p = _ours(model, prompts, capture=False)
+    finally:
+        core.TritonQwen2Attention.fuse_rope = True
+    assert torch.equal(pre_f.last_logits, pre_p.last_logits)
+    assert fused == plain
+
+
 def test_graph_decode_matches_eager(cuda_device):
     model = _model(cuda_device)
     prompts = _prompts()
