@@ -24,13 +24,13 @@
 //   warp 0       TMA producer: both Q tiles, then per key block the 8 K and
 //                8 V pages of this kv head (2 KiB boxes through the block
 //                table) into a 5-stage ring.
-//   warp 1       TMEM owner and single-thread, event-driven MMA issuer:
-//                S_x(j) = Q_x K_j^T as soon as K_j is in and tile x's softmax
-//                has read S_x(j-1); O_x += P_x(j) V_j as soon as tile x
-//                published P_x(j). S_x(j+1) is computed while the softmax of
-//                tile x still works on block j, and neither tile waits behind
-//                the other.
-//   warps 2-3    idle: warpgroup 0 hands most of its registers to the softmax
+//   warps 1, 2   MMA issuers of tile A and tile B (one thread each; warp 1
+//                also owns TMEM): S_x(j) = Q_x K_j^T as soon as K_j is in and
+//                tile x's softmax has read S_x(j-1), then O_x += P_x(j-1)
+//                V_{j-1} once P_x(j-1) is published. S_x(j+1) is computed while
+//                the softmax of tile x still works on block j, and neither
+//                tile's MMAs wait behind the other's issue.
+//   warp 3       idle: warpgroup 0 hands most of its registers to the softmax
 //                warpgroups (setmaxnreg).
 //   warps 4-7    softmax of tile A, warps 8-11 of tile B, one thread per row
 //                (warp w owns TMEM lanes [32 (w % 4), +32)). Per block: the
@@ -86,10 +86,10 @@ constexpr int kPageBoxBytes = kPage * kD * 2;      // 2 KiB
 constexpr int kOffQ = 0;                                   // Q_A, Q_B
 constexpr int kOffKV = kOffQ + 2 * kQBytes;
 constexpr int kOffBar = kOffKV + kStages * kStageBytes;
-// barriers: kv_full[5], kv_empty[5], q_full, mma_done, then per tile:
+// barriers: kv_full[5], kv_empty[5], q_full, mma_done[2], then per tile:
 // s_full, s_free, p_full, pv_done
 constexpr int kTileBars = 4;
-constexpr int kNumBars = 2 * kStages + 2 + 2 * kTileBars;
+constexpr int kNumBars = 2 * kStages + 3 + 2 * kTileBars;
 constexpr int kOffTmemPtr = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = 1024 + kOffTmemPtr + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -128,9 +128,9 @@ struct Bars {
   __device__ uint32_t kv_full(int s) const { return base + 8u * s; }
   __device__ uint32_t kv_empty(int s) const { return base + 8u * (kStages + s); }
   __device__ uint32_t q_full() const { return base + 8u * (2 * kStages); }
-  __device__ uint32_t mma_done() const { return base + 8u * (2 * kStages + 1); }
+  __device__ uint32_t mma_done(int x) const { return base + 8u * (2 * kStages + 1 + x); }
   __device__ uint32_t tile(int x, int i) const {
-    return base + 8u * (2 * kStages + 2 + x * kTileBars + i);
+    return base + 8u * (2 * kStages + 3 + x * kTileBars + i);
   }
   __device__ uint32_t s_full(int x) const { return tile(x, 0); }
   __device__ uint32_t s_free(int x) const { return tile(x, 1); }
@@ -281,10 +281,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bars.kv_full(s), 1);
-      mbar_init(bars.kv_empty(s), 1);
+      mbar_init(bars.kv_empty(s), n_tiles);  // one release per tile
     }
     mbar_init(bars.q_full(), 1);
-    mbar_init(bars.mma_done(), 1);
+    mbar_init(bars.mma_done(0), 1);
+    mbar_init(bars.mma_done(1), 1);
     for (int x = 0; x < 2; ++x) {
       const uint32_t quad_threads = 32u * static_cast<uint32_t>(max(quads_of(x), 1));
       mbar_init(bars.s_full(x), 1);
@@ -376,21 +377,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait(bars.kv_full(j % kStages), static_cast<uint32_t>(j / kStages) & 1u,
                     CIE_DEVERR_WAIT_TIMEOUT);
       }
-    } else if (warp == 1) {
-      // ============================ MMA issuer ================================
-      if (lane == 0) {
+    } else if (warp <= 2) {
+      // ======================= MMA issuers (warp 1: tile A, warp 2: tile B) ===
+      // One thread per tile, in order: S(j) = Q K_j^T as soon as K_j is in and
+      // the softmax has read S(j-1), then O += P(j-1) V_{j-1} once P(j-1) is
+      // published. A tile's QK^T is never queued behind the other tile's P.V
+      // issue, and S(j) goes ahead of PV(j-1), which the softmax needs later.
+      const int x = warp - 1;
+      if (lane == 0 && x < n_tiles) {
         bool ok = mbar_wait(bars.q_full(), 0, CIE_DEVERR_WAIT_TIMEOUT);
-        auto issue_s = [&](int x, int j) {  // S_x(j) = Q_x K_j^T
-          const uint32_t k_tile = sKV + (j % kStages) * kStageBytes;
-#pragma unroll
-          for (int k = 0; k < kD / 16; ++k) {
-            const uint64_t da = smem_desc(sQ + x * kQBytes + k * 32, 16, 1024);
-            const uint64_t db = smem_desc(k_tile + k * 32, 16, 1024);
-            tc_mma_f16(tmem + x * 256 + kColS, da, db, kIdescS, k > 0 ? 1u : 0u);
-          }
-          tc_commit(bars.s_full(x));
+        auto wait = [&](uint32_t bar, uint32_t parity) {
+          if (ok && !mbar_wait(bar, parity, CIE_DEVERR_WAIT_TIMEOUT)) ok = false;
+          return ok;
         };
-        auto issue_pv = [&](int x, int j) {  // O_x (+)= P_x(j) V_j, P from TMEM
+        auto issue_pv = [&](int j) {  // O_x (+)= P_x(j) V_j, P from TMEM
+          if (!wait(bars.p_full(x), static_cast<uint32_t>(j) & 1u)) return;
+          tc_fence_after();
           const uint32_t v_tile = sKV + (j % kStages) * kStageBytes + kKVTileBytes;
 #pragma unroll
           for (int kk = 0; kk < kBlockKeys / 16; ++kk) {
@@ -400,66 +402,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                           (j > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(bars.pv_done(x));
+          tc_commit(bars.kv_empty(j % kStages));  // this tile is done with K_j and V_j
         };
-        // Event-driven issue: S_x(j) once K_j is in and tile x has read
-        // S_x(j-1); PV_x(j) once tile x published P_x(j); stage j is released
-        // when both tiles' PV(j) are issued. test_wait never blocks; an idle
-        // poll naps briefly so the softmax warps sharing this SM
-        // sub-partition keep their issue slots.
-        int ns[2] = {0, 0};
-        int npv[2] = {0, 0};
-        int released = 0;
-        int pv_left = n_blocks * n_tiles;
-        unsigned long long idle_since = 0;
-        while (ok && (pv_left > 0 || released < n_blocks)) {
-          bool progress = false;
+        for (int j = 0; j < n_blocks && ok; ++j) {
+          if (!wait(bars.kv_full(j % kStages), static_cast<uint32_t>(j / kStages) & 1u)) break;
+          if (j > 0 && !wait(bars.s_free(x), static_cast<uint32_t>(j - 1) & 1u)) break;
+          tc_fence_after();
+          const uint32_t k_tile = sKV + (j % kStages) * kStageBytes;
 #pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            if (x >= n_tiles) break;
-            const int j = ns[x];
-            if (j < n_blocks &&
-                mbar_test(bars.kv_full(j % kStages), static_cast<uint32_t>(j / kStages) & 1u) &&
-                (j == 0 || mbar_test(bars.s_free(x), static_cast<uint32_t>(j - 1) & 1u))) {
-              tc_fence_after();
-              issue_s(x, j);
-              ns[x] = j + 1;
-              progress = true;
-            }
+          for (int k = 0; k < kD / 16; ++k) {  // S_x(j) = Q_x K_j^T
+            const uint64_t da = smem_desc(sQ + x * kQBytes + k * 32, 16, 1024);
+            const uint64_t db = smem_desc(k_tile + k * 32, 16, 1024);
+            tc_mma_f16(tmem + x * 256 + kColS, da, db, kIdescS, k > 0 ? 1u : 0u);
           }
-#pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            if (x >= n_tiles) break;
-            const int j = npv[x];
-            if (j < ns[x] && mbar_test(bars.p_full(x), static_cast<uint32_t>(j) & 1u)) {
-              tc_fence_after();
-              issue_pv(x, j);
-              npv[x] = j + 1;
-              --pv_left;
-              progress = true;
-            }
-          }
-          while (released < n_blocks) {
-            const bool all = npv[0] > released && (n_tiles == 1 || npv[1] > released);
-            if (!all) break;
-            tc_commit(bars.kv_empty(released % kStages));
-            ++released;
-            progress = true;
-          }
-          if (progress) {
-            idle_since = 0;
-          } else {
-            const unsigned long long now = global_timer_ns();
-            if (idle_since == 0) idle_since = now;
-            else if (now - idle_since > kWaitLimitNs) {
-              raise_error(CIE_DEVERR_WAIT_TIMEOUT);
-              ok = false;
-            }
-            __nanosleep(32);
-          }
+          tc_commit(bars.s_full(x));
+          if (j > 0) issue_pv(j - 1);
         }
+        if (ok && n_blocks > 0) issue_pv(n_blocks - 1);
         // drain: every MMA this thread issued has completed before TMEM is freed
-        tc_commit(bars.mma_done());
-        mbar_wait(bars.mma_done(), 0, CIE_DEVERR_WAIT_TIMEOUT);
+        tc_commit(bars.mma_done(x));
+        mbar_wait(bars.mma_done(x), 0, CIE_DEVERR_WAIT_TIMEOUT);
       }
       __syncwarp();
     }
