@@ -61,15 +61,10 @@ def decode_attention_noalloc(q, k, v, lens, slot_ids, block_table, out=None,
     return out
 
 
-def mixed_default_splits(batch: int, total_tokens: int, num_kv_heads: int = 2,
-                         device: int = 0) -> int:
-    return int(native.lib().cie_mixed_default_splits(batch, total_tokens, num_kv_heads, device))
-
-
-def mixed_workspace_bytes(total_tokens: int, num_q_heads: int, head_dim: int,
-                          num_splits: int) -> int:
-    return int(native.lib().cie_mixed_workspace_bytes(total_tokens, num_q_heads, head_dim,
-                                                        num_splits))
+def mixed_workspace_bytes(batch: int, total_tokens: int, num_kv_heads: int = 2,
+                          num_splits: int = 0, device: int = 0) -> int:
+    return int(native.lib().cie_mixed_workspace_bytes(batch, total_tokens, num_kv_heads,
+                                                        num_splits, device))
 
 
 def mixed_attention(q, k, v, max_seqlen: int, cu_seqlens, kv_lens, slot_ids, block_table,
@@ -78,19 +73,17 @@ def mixed_attention(q, k, v, max_seqlen: int, cu_seqlens, kv_lens, slot_ids, blo
     """cie_mixed_attention; rows outside every sequence are left as they were in ``out``."""
     B = slot_ids.shape[0]
     T = q.shape[1]
-    S = num_splits if num_splits > 0 else mixed_default_splits(B, T, k.shape[1],
-                                                               q.device.index or 0)
     if out is None:
         out = torch.empty_like(q)
-    need = mixed_workspace_bytes(T, q.shape[2], q.shape[3], S)
-    if need > 0 and workspace is None:
-        workspace = torch.empty(need // 4, dtype=torch.float32, device=q.device)
+    if workspace is None:
+        need = mixed_workspace_bytes(B, T, k.shape[1], num_splits, q.device.index or 0)
+        workspace = torch.empty(max(need // 4, 1), dtype=torch.float32, device=q.device)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     st = native.lib().cie_mixed_attention(
         _p(q), _p(k), _p(v), int(max_seqlen), _p(cu_seqlens), _p(kv_lens), _p(slot_ids),
         _p(block_table), _p(out), _p(workspace), ws_bytes, B, T, q.shape[2], k.shape[1],
         q.shape[3], k.shape[2], k.shape[0], block_table.shape[0], block_table.stride(0),
-        k.stride(0), k.stride(1), S, native.stream_ptr(stream))
+        k.stride(0), k.stride(1), num_splits, native.stream_ptr(stream))
     native.check(st, "cie_mixed_attention")
     return out
 

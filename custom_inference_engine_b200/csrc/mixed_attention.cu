@@ -68,7 +68,12 @@ constexpr int kBlockKeys = 128;
 constexpr int kPagesPerBlock = kBlockKeys / kPage;  // 8
 constexpr int kStages = 5;
 constexpr int kMinBlocksPerSplit = 2;
-constexpr int kMaxSplits = 16;
+constexpr int kMaxSplits = 16;      // num_splits >= 1: key ranges per tile pair at most
+constexpr int kMaxPieces = 16;      // automatic plan: key ranges per tile pair at most
+constexpr int kWaves = 1;           // automatic plan: pieces of about 1/SMs of the work
+constexpr int kPlanThreads = 1024;  // the planning kernel is one CTA
+constexpr int kPlanMaxBatch = 2048;
+constexpr int kSizeBuckets = kPlanThreads;  // pieces ordered by key blocks, largest first
 constexpr int kTileThreads = 128;                   // softmax threads per tile, one per row
 constexpr int kThreads = 128 + 2 * kTileThreads;    // warpgroup 0 + one per tile
 // Register split after launch (launch: 384 x 168): warpgroup 0 drops to 56,
@@ -102,26 +107,43 @@ constexpr uint32_t kColO = 192;
 constexpr uint32_t kIdescS = idesc_f16_f32(kM, kBlockKeys, false);
 constexpr uint32_t kIdescPV = idesc_f16_f32(kM, kD, true);
 
+// partial record of one row: unnormalised O[64], m (log2 units: max of score
+// * scale * log2(e)), l
+constexpr int kPartFloats = kD + 2;
+constexpr int kRecRows = 2 * kRows;  // one record = the rows of both tiles of a pair
+
+// The work plan, in the caller's workspace. A work item is one CTA: a tile
+// pair of one (sequence, kv head) and a contiguous range of its key blocks.
+// Items are stored largest range first, two int4 each:
+//   {b, pair | kv_head << 16, first block, blocks}, {record, split, piece, pieces}.
+// A pair cut into `pieces` ranges owns records [record, record + pieces) and
+// the counter counters[split]; its last piece to finish merges the others.
+struct Plan {
+  int* header;         // [0] items
+  int4* items;
+  unsigned* counters;  // per split pair: pieces finished
+  float* records;      // [record][kRecRows][kPartFloats]
+  int max_items, max_split, max_rec;
+};
+
 struct Params {
   const int64_t* cu_seqlens;
   const int64_t* kv_lens;
   const int64_t* slot_ids;
   const int64_t* block_table;
   __half* o;
-  float* part;  // [split][token][q head] x (acc[64], m, l), only when splits > 1
+  Plan plan;
   int64_t total_tokens;
   int64_t max_seqlen;
   int64_t n_pages;
   int64_t n_slots;
   int64_t bt_stride;
+  int batch;
   int num_q_heads;
   int num_kv_heads;
-  int num_splits;
+  int num_splits;  // <= 0: automatic plan
+  int n_sm;
 };
-
-// partial record: unnormalised O[64], m (log2 units: max of score * scale *
-// log2(e)), l
-constexpr int kPartFloats = kD + 2;
 
 struct Bars {
   uint32_t base;
@@ -218,51 +240,265 @@ constexpr unsigned kPolyPairs = 0x88u;
 
 // ---- the work decomposition, shared with the merge kernel -------------------
 
+struct SeqInfo {
+  int L;       // chunk length
+  int kv_len;  // cached keys before the chunk
+  bool valid;
+};
+
+// Sequence b's chunk; invalid (and, with `report`, a device error) when its
+// row range, slot or length is out of bounds.
+__device__ __forceinline__ SeqInfo seq_info(const Params& p, int b, bool report) {
+  SeqInfo si{0, 0, false};
+  // all four loads issued before any of them is tested
+  const int64_t start = p.cu_seqlens[b];
+  const int64_t end = p.cu_seqlens[b + 1];
+  const int64_t slot = p.slot_ids[b];
+  int64_t kv_len = p.kv_lens[b];
+  if (start < 0 || end < start || end > p.total_tokens) {
+    if (report) raise_error(CIE_DEVERR_BAD_SEQLENS);
+    return si;
+  }
+  const int64_t L64 = end - start;
+  if (L64 > p.max_seqlen) {
+    if (report) raise_error(CIE_DEVERR_BAD_SEQLENS);
+    return si;
+  }
+  if (L64 == 0) return si;
+  if (slot < 0 || slot >= p.n_slots) {
+    if (report) raise_error(CIE_DEVERR_BAD_SLOT);
+    return si;
+  }
+  if (kv_len < 0) kv_len = 0;
+  if ((kv_len + L64 + kPage - 1) / kPage > p.bt_stride) {
+    if (report) raise_error(CIE_DEVERR_BAD_LENGTH);
+    return si;
+  }
+  si.L = static_cast<int>(L64);
+  si.kv_len = static_cast<int>(kv_len);
+  si.valid = true;
+  return si;
+}
+
+// key blocks the last row of tile pair `pair` needs
+__device__ __forceinline__ int pair_blocks(int L, int kv_len, int pair) {
+  const int end = min(L, (pair + 1) * kPairTokens);
+  return (kv_len + end + kBlockKeys - 1) / kBlockKeys;
+}
+
 struct PairInfo {
   int L;            // chunk length of the sequence
   int tok0;         // first token of the pair inside the chunk
   int pair_tokens;  // tokens of the pair (1..36)
   int kv_len;
   int n_blocks;     // key blocks the pair's last row needs
-  int bps;          // blocks per split
-  int n_active;     // splits that own at least one block
   bool valid;
 };
 
-__device__ __forceinline__ PairInfo pair_info(const Params& p, int b, int pair, bool report) {
+__device__ __forceinline__ PairInfo pair_info(const Params& p, int b, int pair) {
   PairInfo pi{};
   pi.valid = false;
-  const int64_t start = p.cu_seqlens[b];
-  const int64_t end = p.cu_seqlens[b + 1];
-  if (start < 0 || end < start || end > p.total_tokens) {
-    if (report) raise_error(CIE_DEVERR_BAD_SEQLENS);
-    return pi;
-  }
-  const int64_t L64 = end - start;
-  if (report && pair == 0 && L64 > p.max_seqlen) raise_error(CIE_DEVERR_BAD_SEQLENS);
+  const SeqInfo si = seq_info(p, b, false);
+  if (!si.valid) return pi;
   const int tok0 = pair * kPairTokens;
-  if (tok0 >= L64) return pi;
-  const int64_t slot = p.slot_ids[b];
-  if (slot < 0 || slot >= p.n_slots) {
-    if (report) raise_error(CIE_DEVERR_BAD_SLOT);
-    return pi;
-  }
-  int64_t kv_len = p.kv_lens[b];
-  if (kv_len < 0) kv_len = 0;
-  if ((kv_len + L64 + kPage - 1) / kPage > p.bt_stride) {
-    if (report) raise_error(CIE_DEVERR_BAD_LENGTH);
-    return pi;
-  }
-  pi.L = static_cast<int>(L64);
+  if (tok0 >= si.L) return pi;
+  pi.L = si.L;
   pi.tok0 = tok0;
   pi.pair_tokens = min(pi.L - tok0, kPairTokens);
-  pi.kv_len = static_cast<int>(kv_len);
-  const int n_keys = pi.kv_len + tok0 + pi.pair_tokens;
-  pi.n_blocks = (n_keys + kBlockKeys - 1) / kBlockKeys;
-  pi.bps = max((pi.n_blocks + p.num_splits - 1) / p.num_splits, kMinBlocksPerSplit);
-  pi.n_active = (pi.n_blocks + pi.bps - 1) / pi.bps;
+  pi.kv_len = si.kv_len;
+  pi.n_blocks = pair_blocks(si.L, si.kv_len, pair);
   pi.valid = true;
   return pi;
+}
+
+// Exclusive prefix sum over the kPlanThreads threads of a CTA; `total`
+// receives the sum. Every thread must call it.
+__device__ __forceinline__ int plan_excl_scan(int v, int* s_warp, int& total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int t = lane < kPlanThreads / 32 ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    s_warp[lane] = t;
+  }
+  __syncthreads();
+  const int before = (w > 0 ? s_warp[w - 1] : 0) + x - v;
+  total = s_warp[kPlanThreads / 32 - 1];
+  __syncthreads();
+  return before;
+}
+
+// The work plan (one CTA). Units are (sequence, tile pair, kv head); a unit of
+// nb key blocks becomes k pieces of balanced key ranges: with num_splits >= 1
+// k = ceil(nb / max(ceil(nb / num_splits), 2)); automatically, ranges of at
+// most C = max(2, ceil(total blocks / (SMs * kWaves))) blocks, k <= kMaxPieces.
+// Pieces are written largest first (a counting sort on their block count), so
+// the longest CTAs start first and the short ones fill the tail. Sequences
+// whose rows, slot or length are out of bounds raise a device error here and
+// get no work.
+__global__ void __launch_bounds__(kPlanThreads) mixed_plan_kernel(const Params p) {
+  __shared__ int s_pfx[kPlanMaxBatch + 1];  // tile pairs before sequence b
+  __shared__ int s_len[kPlanMaxBatch];
+  __shared__ int s_kv[kPlanMaxBatch];
+  __shared__ int s_bkt[kSizeBuckets];
+  __shared__ int s_warp[32];
+  __shared__ unsigned long long s_blocks;
+  __shared__ int s_cnt[3];  // items, split pairs, records
+  // the attention grid may be scheduled now; it waits for this grid to finish
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int tid = threadIdx.x;
+  const int B = p.batch;
+  const int H = p.num_kv_heads;
+  if (tid == 0) {
+    s_blocks = 0;
+    s_cnt[0] = s_cnt[1] = s_cnt[2] = 0;
+  }
+  for (int i = tid; i < kSizeBuckets; i += kPlanThreads) s_bkt[i] = 0;
+  int carry = 0;
+  for (int base = 0; base < B; base += kPlanThreads) {
+    const int b = base + tid;
+    SeqInfo si{0, 0, false};
+    if (b < B) si = seq_info(p, b, true);
+    const int P = si.valid ? (si.L + kPairTokens - 1) / kPairTokens : 0;
+    int tot;
+    const int before = plan_excl_scan(P, s_warp, tot);
+    if (b < B) {
+      s_pfx[b] = carry + before;
+      s_len[b] = si.L;
+      s_kv[b] = si.kv_len;
+    }
+    carry += tot;
+  }
+  if (tid == 0) s_pfx[B] = carry;
+  __syncthreads();
+  const int n_units = carry * H;
+  // unit g: pair g / H (sequences in order, pairs in order), kv head g % H
+  auto unit = [&](int g, int& b, int& pair, int& h) {
+    h = g % H;
+    const int gp = g / H;
+    int lo = 0, hi = B - 1;  // the last b with s_pfx[b] <= gp owns pair gp
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_pfx[mid] <= gp) lo = mid;
+      else hi = mid - 1;
+    }
+    b = lo;
+    pair = gp - s_pfx[lo];
+    return pair_blocks(s_len[lo], s_kv[lo], pair);
+  };
+  unsigned long long mine = 0;
+  for (int g = tid; g < n_units; g += kPlanThreads) {
+    int b, pair, h;
+    mine += static_cast<unsigned long long>(unit(g, b, pair, h));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+  if ((tid & 31) == 0 && mine != 0) atomicAdd(&s_blocks, mine);
+  __syncthreads();
+  const long long total_blocks = static_cast<long long>(s_blocks);
+  const long long slots = static_cast<long long>(p.n_sm) * kWaves;
+  const long long C = max(static_cast<long long>(kMinBlocksPerSplit), (total_blocks + slots - 1) / slots);
+  auto pieces_of = [&](int nb) {
+    if (p.num_splits <= 0) return static_cast<int>(min(static_cast<long long>(kMaxPieces), (nb + C - 1) / C));
+    const int bps = max((nb + p.num_splits - 1) / p.num_splits, kMinBlocksPerSplit);
+    return (nb + bps - 1) / bps;
+  };
+  auto bucket = [](int blocks) { return min(blocks, kSizeBuckets - 1); };
+  for (int g = tid; g < n_units; g += kPlanThreads) {
+    int b, pair, h;
+    const int nb = unit(g, b, pair, h);
+    const int k = pieces_of(nb);
+    for (int i = 0; i < k; ++i)
+      atomicAdd(&s_bkt[bucket(nb * (i + 1) / k - nb * i / k)], 1);
+  }
+  __syncthreads();
+  {  // bucket cursors: items of larger ranges first
+    const int bk = kSizeBuckets - 1 - tid;
+    const int c = s_bkt[bk];
+    int tot;
+    const int before = plan_excl_scan(c, s_warp, tot);
+    s_bkt[bk] = before;
+    if (tid == 0) s_cnt[0] = tot;
+  }
+  __syncthreads();
+  for (int g = tid; g < n_units; g += kPlanThreads) {
+    int b, pair, h;
+    const int nb = unit(g, b, pair, h);
+    const int k = pieces_of(nb);
+    int split = -1, rec = -1;
+    bool dead = false;
+    if (k > 1) {
+      split = atomicAdd(&s_cnt[1], 1);
+      rec = atomicAdd(&s_cnt[2], k);
+      if (split < p.plan.max_split && rec + k <= p.plan.max_rec) {
+        p.plan.counters[split] = 0u;
+      } else {  // outside the host's bounds (cannot happen): no work, an error
+        raise_error(CIE_DEVERR_BAD_LENGTH);
+        dead = true;
+      }
+    }
+    for (int i = 0; i < k; ++i) {
+      const int lo = nb * i / k;
+      const int n = nb * (i + 1) / k - lo;
+      const int pos = atomicAdd(&s_bkt[bucket(n)], 1);
+      if (pos >= p.plan.max_items) {
+        raise_error(CIE_DEVERR_BAD_LENGTH);
+        continue;
+      }
+      p.plan.items[2 * pos] = make_int4(b, pair | (h << 16), lo, dead ? 0 : n);
+      p.plan.items[2 * pos + 1] = make_int4(rec, split, i, k);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) p.plan.header[0] = min(s_cnt[0], p.plan.max_items);
+}
+
+// Combines the records of one row of a split tile pair (every piece's
+// record, this CTA's included, is written before the last piece gets here):
+// O = sum_q w_q acc_q / sum_q w_q l_q with w_q = 2^(m_q - max m), m in log2
+// units. Out of line, so that its registers do not weigh on the softmax loop.
+__device__ __noinline__ void merge_row(const float* rec0, int n_pieces, __half* dst) {
+  constexpr int64_t kStride = static_cast<int64_t>(kRecRows) * kPartFloats;
+  float M = -CUDART_INF_F;
+  for (int q = 0; q < n_pieces; ++q) M = fmaxf(M, __ldcg(rec0 + q * kStride + kD));
+  float acc[kD];
+#pragma unroll
+  for (int d = 0; d < kD; ++d) acc[d] = 0.f;
+  float den = 0.f;
+  for (int q = 0; q < n_pieces; ++q) {
+    const float* rec = rec0 + q * kStride;
+    const float mq = __ldcg(rec + kD);
+    if (mq == -CUDART_INF_F) continue;  // no visible key in this piece's range
+    const float w = ex2(mq - M);
+    den += w * __ldcg(rec + kD + 1);
+#pragma unroll
+    for (int cc = 0; cc < kD / 2; ++cc) {
+      const float2 a = __ldcg(reinterpret_cast<const float2*>(rec) + cc);
+      acc[2 * cc] += w * a.x;
+      acc[2 * cc + 1] += w * a.y;
+    }
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+#pragma unroll
+  for (int cc = 0; cc < kD / 8; ++cc) {
+    uint4 w;
+    w.x = pack_half2(acc[cc * 8 + 0] * inv, acc[cc * 8 + 1] * inv);
+    w.y = pack_half2(acc[cc * 8 + 2] * inv, acc[cc * 8 + 3] * inv);
+    w.z = pack_half2(acc[cc * 8 + 4] * inv, acc[cc * 8 + 5] * inv);
+    w.w = pack_half2(acc[cc * 8 + 6] * inv, acc[cc * 8 + 7] * inv);
+    reinterpret_cast<uint4*>(dst)[cc] = w;
+  }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -277,23 +513,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sKV = sbase + kOffKV;
   const Bars bars{sbase + kOffBar};
   uint32_t* tmem_ptr_smem = reinterpret_cast<uint32_t*>(smem + kOffTmemPtr);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + kOffTmemPtr + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int h = blockIdx.x % p.num_kv_heads;
-  const int b = blockIdx.x / p.num_kv_heads;
-  const int pair = gridDim.y - 1 - blockIdx.y;
-  const int split = blockIdx.z;
-
-  const PairInfo pi = pair_info(p, b, pair, threadIdx.x == 0 && split == 0);
-  if (!pi.valid || split >= pi.n_active) return;
+  // the plan is written by the planning grid, which this launch depends on
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (static_cast<int>(blockIdx.x) >= p.plan.header[0]) return;
+  const int4 item = p.plan.items[2 * blockIdx.x];
+  const int4 item_m = p.plan.items[2 * blockIdx.x + 1];
+  const int b = item.x;
+  const int pair = item.y & 0xffff;
+  const int h = static_cast<int>(static_cast<unsigned>(item.y) >> 16);
+  const int blk0 = item.z;      // first key block of this CTA
+  const int n_blocks = item.w;  // key blocks of this CTA
+  if (n_blocks <= 0) return;
+  const PairInfo pi = pair_info(p, b, pair);
+  if (!pi.valid) return;
   const int64_t start = p.cu_seqlens[b];
   const int64_t slot = p.slot_ids[b];
-  const int blk0 = split * pi.bps;                          // first key block of this CTA
-  const int n_blocks = min(pi.n_blocks, blk0 + pi.bps) - blk0;
   const int n_keys = pi.kv_len + pi.tok0 + pi.pair_tokens;  // keys of the pair's last row
   const int n_valid_pages = (n_keys + kPage - 1) / kPage;
-  const bool direct = pi.n_active == 1;                     // write O, no partial
+  const bool direct = item_m.w == 1;                        // write O, no partial
   const int n_tiles = pi.pair_tokens > kTileTokens ? 2 : 1;
   // lane quadrants of tile x whose rows [0, 7 * tokens) hold any real token
   auto quads_of = [&](int x) {
@@ -317,9 +558,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bars.pv_done(x), 1);
     }
     fence_mbar_init();
-    // the merge kernel (programmatic stream serialization) may be scheduled
-    // once every CTA of this grid has started; it waits for our completion
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   }
   // Rows 126 and 127 of each Q tile are never loaded, and tile B's box is
   // skipped when the pair has one tile: zero what TMA will not write so the
@@ -601,34 +839,62 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_32x32b_x32(t_o, *reinterpret_cast<uint32_t(*)[32]>(&ob[0]));
       tmem_ld_32x32b_x32(t_o + 32, *reinterpret_cast<uint32_t(*)[32]>(&ob[32]));
       tc_wait_ld();
-      if (ok && row_valid) {
-        const int64_t tok = start + tile_tok0 + tok_in_tile;
-        const int hq = h * kGroup + head_in_group;
-        if (direct) {
-          const float inv = 1.f / l_run;
-          __half* dst = p.o + (tok * p.num_q_heads + hq) * kD;
+      const int64_t tok = start + tile_tok0 + tok_in_tile;
+      const int hq = h * kGroup + head_in_group;
+      auto store_o = [&](float inv) {
+        __half* dst = p.o + (tok * p.num_q_heads + hq) * kD;
 #pragma unroll
-          for (int cc = 0; cc < kD / 8; ++cc) {
-            uint4 w;
-            w.x = pack_half2(__uint_as_float(ob[cc * 8 + 0]) * inv,
-                             __uint_as_float(ob[cc * 8 + 1]) * inv);
-            w.y = pack_half2(__uint_as_float(ob[cc * 8 + 2]) * inv,
-                             __uint_as_float(ob[cc * 8 + 3]) * inv);
-            w.z = pack_half2(__uint_as_float(ob[cc * 8 + 4]) * inv,
-                             __uint_as_float(ob[cc * 8 + 5]) * inv);
-            w.w = pack_half2(__uint_as_float(ob[cc * 8 + 6]) * inv,
-                             __uint_as_float(ob[cc * 8 + 7]) * inv);
-            reinterpret_cast<uint4*>(dst)[cc] = w;
-          }
-        } else {
-          float* rec = p.part + ((static_cast<int64_t>(split) * p.total_tokens + tok) *
-                                     p.num_q_heads + hq) * kPartFloats;
+        for (int cc = 0; cc < kD / 8; ++cc) {
+          uint4 w;
+          w.x = pack_half2(__uint_as_float(ob[cc * 8 + 0]) * inv,
+                           __uint_as_float(ob[cc * 8 + 1]) * inv);
+          w.y = pack_half2(__uint_as_float(ob[cc * 8 + 2]) * inv,
+                           __uint_as_float(ob[cc * 8 + 3]) * inv);
+          w.z = pack_half2(__uint_as_float(ob[cc * 8 + 4]) * inv,
+                           __uint_as_float(ob[cc * 8 + 5]) * inv);
+          w.w = pack_half2(__uint_as_float(ob[cc * 8 + 6]) * inv,
+                           __uint_as_float(ob[cc * 8 + 7]) * inv);
+          reinterpret_cast<uint4*>(dst)[cc] = w;
+        }
+      };
+      if (direct) {
+        if (ok && row_valid) store_o(1.f / l_run);
+      } else {
+        // This piece's partial (m = -inf when its key range had no visible
+        // key for the row). The last piece of the pair to finish combines
+        // all of them: O = sum_q w_q acc_q / sum_q w_q l_q, w_q = 2^(m_q - max m).
+        // the item's split fields, read again here rather than kept live
+        // through the softmax loop
+        int4 im;
+        asm volatile("ld.global.cg.v4.s32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(im.x), "=r"(im.y), "=r"(im.z), "=r"(im.w)
+                     : "l"(p.plan.items + 2 * blockIdx.x + 1));
+        const int rec0 = im.x, split = im.y, piece = im.z, n_pieces = im.w;
+        if (row_valid) {
+          float* rec = p.plan.records +
+                       (static_cast<int64_t>(rec0 + piece) * kRecRows + x * kRows + row) * kPartFloats;
 #pragma unroll
           for (int cc = 0; cc < kD / 2; ++cc)
             reinterpret_cast<float2*>(rec)[cc] =
                 make_float2(__uint_as_float(ob[cc * 2 + 0]), __uint_as_float(ob[cc * 2 + 1]));
-          rec[kD] = m_ref;  // -inf when this key range had no visible key for the row
+          rec[kD] = m_ref;
           rec[kD + 1] = l_run;
+        }
+        __threadfence();
+        // every working softmax thread of both tiles has published its rows
+        const uint32_t n_thr = 32u * static_cast<uint32_t>(quads_of(0) + quads_of(1));
+        asm volatile("bar.sync 1, %0;" ::"r"(n_thr) : "memory");
+        if (warp == 4 && lane == 0)
+          *last_flag = atomicAdd(p.plan.counters + split, 1u) ==
+                               static_cast<unsigned>(n_pieces - 1)
+                           ? 1
+                           : 0;
+        asm volatile("bar.sync 1, %0;" ::"r"(n_thr) : "memory");
+        if (*last_flag != 0 && row_valid && ok) {
+          __threadfence();
+          merge_row(p.plan.records + (static_cast<int64_t>(rec0) * kRecRows + x * kRows + row) *
+                                         kPartFloats,
+                    n_pieces, p.o + (tok * p.num_q_heads + hq) * kD);
         }
       }
     }
@@ -640,50 +906,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-// Combines the key-range partials of the tile pairs that were split: per row,
-// O = sum_s w_s acc_s / sum_s w_s l_s with w_s = 2^(m_s - max m), m in log2
-// units. One warp per row (blockIdx.z picks 8 rows of the pair): lane
-// s < splits loads (m_s, l_s) so the maximum and the denominator are warp
-// reductions, then every lane accumulates two output columns over the splits. Launched with programmatic
-// stream serialization: griddepcontrol.wait holds it until the attention
-// kernel has finished and its writes are visible.
-__global__ void __launch_bounds__(256) mixed_merge_kernel(const Params p) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int h = blockIdx.x % p.num_kv_heads;
-  const int b = blockIdx.x / p.num_kv_heads;
-  const int pair = blockIdx.y;
-  const PairInfo pi = pair_info(p, b, pair, false);
-  if (!pi.valid || pi.n_active <= 1) return;
-  const int r = blockIdx.z * 8 + (threadIdx.x >> 5);
-  if (r >= pi.pair_tokens * kGroup) return;
-  const int lane = threadIdx.x & 31;
-  const int64_t tok = p.cu_seqlens[b] + pi.tok0 + r / kGroup;
-  const int hq = h * kGroup + r % kGroup;
-  const int64_t split_stride = p.total_tokens * p.num_q_heads * kPartFloats;
-  const float* rec0 = p.part + (tok * p.num_q_heads + hq) * kPartFloats;
-  float m = -CUDART_INF_F, l = 0.f;
-  if (lane < pi.n_active) {
-    m = rec0[lane * split_stride + kD];
-    l = rec0[lane * split_stride + kD + 1];
+// Workspace layout: the plan header, the items, the split counters and the
+// partial records, each section 256-byte aligned. The bounds hold for any
+// lengths: a sequence has at most ceil(L / 36) <= L / 36 + 1 tile pairs; with
+// num_splits = S every pair is cut into at most S pieces; automatically a
+// pair of nb blocks gets at most nb / C + 1 pieces and only pairs longer than
+// C (fewer than total / C <= SMs * kWaves of them) are cut, so the pieces of
+// cut pairs number at most 2 * SMs * kWaves.
+struct PlanSizes {
+  int64_t items, split, rec;
+  size_t off_items, off_counters, off_records, bytes;
+};
+
+inline size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+inline PlanSizes plan_sizes(int batch, int64_t total_tokens, int num_kv_heads, int num_splits,
+                            int n_sm) {
+  PlanSizes ps{};
+  const int64_t units =
+      static_cast<int64_t>(num_kv_heads) * ((total_tokens + kPairTokens - 1) / kPairTokens + batch);
+  if (num_splits >= 1) {
+    ps.items = num_splits * units;
+    ps.split = num_splits > 1 ? units : 0;
+    ps.rec = num_splits > 1 ? num_splits * units : 0;
+  } else {
+    const int64_t slots = static_cast<int64_t>(n_sm) * kWaves;
+    ps.items = units + slots;
+    ps.split = slots;
+    ps.rec = 2 * slots;
   }
-  float M = m;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  const float w = (lane < pi.n_active && m != -CUDART_INF_F) ? ex2(m - M) : 0.f;
-  float den = w * l;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-  float2 num = make_float2(0.f, 0.f);
-  for (int s = 0; s < pi.n_active; ++s) {
-    const float ws = __shfl_sync(0xffffffffu, w, s);
-    if (ws == 0.f) continue;
-    const float2 a = *reinterpret_cast<const float2*>(rec0 + s * split_stride + 2 * lane);
-    num.x += ws * a.x;
-    num.y += ws * a.y;
-  }
-  const float inv = den > 0.f ? 1.f / den : 0.f;
-  *reinterpret_cast<__half2*>(p.o + (tok * p.num_q_heads + hq) * kD + 2 * lane) =
-      __floats2half2_rn(num.x * inv, num.y * inv);
+  ps.off_items = 256;
+  ps.off_counters = ps.off_items + round256(static_cast<size_t>(ps.items) * 2 * sizeof(int4));
+  ps.off_records = ps.off_counters + round256(static_cast<size_t>(ps.split) * sizeof(unsigned));
+  ps.bytes = ps.off_records +
+             static_cast<size_t>(ps.rec) * kRecRows * kPartFloats * sizeof(float);
+  return ps;
+}
+
+inline int device_sms(int device) {
+  int n = 0;
+  if (device >= 0 &&
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && n > 0)
+    return n;
+  return 148;
 }
 
 }  // namespace mixed
@@ -691,31 +956,11 @@ __global__ void __launch_bounds__(256) mixed_merge_kernel(const Params p) {
 
 extern "C" {
 
-int cie_mixed_default_splits(int batch, int64_t total_tokens, int num_kv_heads, int device) {
+size_t cie_mixed_workspace_bytes(int batch, int64_t total_tokens, int num_kv_heads,
+                                 int num_splits, int device) {
   using namespace cie::mixed;
-  int sms = 148;
-  if (device >= 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && n > 0)
-      sms = n;
-  }
-  if (batch <= 0 || total_tokens <= 0 || num_kv_heads <= 0) return 1;
-  // Tile-pair CTAs without splitting: at least one per non-empty sequence and
-  // one per 36 tokens. A CTA pays a fixed pipeline fill, so key ranges are
-  // split only while the grid would leave SMs idle.
-  const int64_t pairs = (total_tokens + kPairTokens - 1) / kPairTokens;
-  const int64_t units = static_cast<int64_t>(num_kv_heads) * (pairs > batch ? pairs : batch);
-  int64_t s = sms / units;
-  if (s < 1) s = 1;
-  if (s > kMaxSplits) s = kMaxSplits;
-  return static_cast<int>(s);
-}
-
-size_t cie_mixed_workspace_bytes(int64_t total_tokens, int num_q_heads, int head_dim,
-                                 int num_splits) {
-  if (total_tokens <= 0 || num_splits <= 1 || num_q_heads <= 0 || head_dim <= 0) return 0;
-  return static_cast<size_t>(num_splits) * static_cast<size_t>(total_tokens) * num_q_heads *
-         (static_cast<size_t>(head_dim) + 2) * sizeof(float);
+  if (batch < 0 || total_tokens < 0 || num_kv_heads < 1) return 0;
+  return plan_sizes(batch, total_tokens, num_kv_heads, num_splits, device_sms(device)).bytes;
 }
 
 int cie_mixed_attention(const void* q, const void* k, const void* v, int64_t max_seqlen,
@@ -755,17 +1000,18 @@ int cie_mixed_attention(const void* q, const void* k, const void* v, int64_t max
   if ((kv_page_stride % 8) || (kv_head_stride % 8) || !aligned16(k) || !aligned16(v) ||
       !aligned16(q) || !aligned16(o))
     return fail(CIE_ERR_ALIGNMENT, "q/o/k/v must be 16-byte aligned with 16-byte strides");
-  const int S = num_splits > 0 ? num_splits
-                               : cie_mixed_default_splits(batch, total_tokens, num_kv_heads,
-                                                          current_device());
-  if (S > kMaxSplits) return fail(CIE_ERR_INVALID_ARGUMENT, "num_splits %d > %d", S, kMaxSplits);
-  if (S > 1) {
-    const size_t need = cie_mixed_workspace_bytes(total_tokens, num_q_heads, head_dim, S);
-    if (workspace == nullptr || workspace_bytes < need)
-      return fail(CIE_ERR_WORKSPACE, "split path needs %zu workspace bytes, got %zu", need,
-                  workspace == nullptr ? size_t(0) : workspace_bytes);
-    if (!aligned16(workspace)) return fail(CIE_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
-  }
+  if (num_splits > kMaxSplits)
+    return fail(CIE_ERR_INVALID_ARGUMENT, "num_splits %d > %d", num_splits, kMaxSplits);
+  if (batch > kPlanMaxBatch)
+    return fail(CIE_ERR_UNSUPPORTED, "batch %d > %d sequences", batch, kPlanMaxBatch);
+  if (num_kv_heads > 32767) return fail(CIE_ERR_UNSUPPORTED, "num_kv_heads %d", num_kv_heads);
+  const int n_sm = sm_count();
+  const PlanSizes ps = plan_sizes(batch, total_tokens, num_kv_heads, num_splits, n_sm);
+  if (ps.items > 0x7fffffff) return fail(CIE_ERR_OVERFLOW, "too many work items");
+  if (workspace == nullptr || workspace_bytes < ps.bytes)
+    return fail(CIE_ERR_WORKSPACE, "mixed attention needs %zu workspace bytes, got %zu", ps.bytes,
+                workspace == nullptr ? size_t(0) : workspace_bytes);
+  if (!aligned16(workspace)) return fail(CIE_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
 
   CUtensorMap tm_q, tm_k, tm_v;
   {
@@ -801,36 +1047,42 @@ int cie_mixed_attention(const void* q, const void* k, const void* v, int64_t max
   p.slot_ids = slot_ids;
   p.block_table = block_table;
   p.o = static_cast<__half*>(o);
-  p.part = S > 1 ? static_cast<float*>(workspace) : nullptr;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.plan.header = reinterpret_cast<int*>(ws);
+  p.plan.items = reinterpret_cast<int4*>(ws + ps.off_items);
+  p.plan.counters = reinterpret_cast<unsigned*>(ws + ps.off_counters);
+  p.plan.records = reinterpret_cast<float*>(ws + ps.off_records);
+  p.plan.max_items = static_cast<int>(ps.items);
+  p.plan.max_split = static_cast<int>(ps.split);
+  p.plan.max_rec = static_cast<int>(ps.rec);
   p.total_tokens = total_tokens;
   p.max_seqlen = max_seqlen;
   p.n_pages = n_pages;
   p.n_slots = n_slots;
   p.bt_stride = bt_stride;
+  p.batch = batch;
   p.num_q_heads = num_q_heads;
   p.num_kv_heads = num_kv_heads;
-  p.num_splits = S;
+  p.num_splits = num_splits;
+  p.n_sm = n_sm;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // x: (sequence, kv head); y: tile pair, walked last-pair-first; z: key range
-  dim3 grid(static_cast<unsigned>(batch * num_kv_heads), static_cast<unsigned>(n_pairs), S);
-  mixed_attention_kernel<<<grid, kThreads, kSmemBytes, s>>>(tm_q, tm_k, tm_v, p);
+  mixed_plan_kernel<<<1, kPlanThreads, 0, s>>>(p);
   cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "mixed plan launch: %s", cudaGetErrorString(e));
+  // one CTA per item (the plan holds at most ps.items; the rest return at
+  // once); scheduled while the plan is made, waiting for it in griddepcontrol.wait
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(ps.items));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, mixed_attention_kernel, tm_q, tm_k, tm_v, p);
   if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "mixed launch: %s", cudaGetErrorString(e));
-  if (S > 1) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(batch * num_kv_heads), static_cast<unsigned>(n_pairs),
-                       (2 * kRows + 7) / 8);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, mixed_merge_kernel, p);
-    if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "mixed merge launch: %s", cudaGetErrorString(e));
-  }
   return CIE_OK;
 }
 

@@ -112,21 +112,19 @@ at::Tensor gqa_mixed_attention(const at::Tensor& q, const at::Tensor& k, const a
               "cu_seqlens / kv_lens / slot_ids must be contiguous");
   c10::cuda::CUDAGuard guard(q.device());
   at::Tensor o = at::empty_like(q);
-  const int S = cie_mixed_default_splits(static_cast<int>(B), q.size(1),
-                                         static_cast<int>(k.size(1)), q.get_device());
-  const size_t ws_bytes = cie_mixed_workspace_bytes(q.size(1), static_cast<int>(q.size(2)),
-                                                    static_cast<int>(q.size(3)), S);
-  at::Tensor ws;
-  if (ws_bytes > 0)
-    ws = at::empty({static_cast<int64_t>(ws_bytes / sizeof(float))},
-                   q.options().dtype(at::kFloat));
+  // the work plan and the partials of split tile pairs (automatic plan)
+  const size_t ws_bytes = cie_mixed_workspace_bytes(static_cast<int>(B), q.size(1),
+                                                    static_cast<int>(k.size(1)), 0,
+                                                    q.get_device());
+  at::Tensor ws = at::empty({static_cast<int64_t>((ws_bytes + 3) / sizeof(float))},
+                            q.options().dtype(at::kFloat));
   const int st = cie_mixed_attention(
       q.data_ptr(), k.data_ptr(), v.data_ptr(), max_seqlen, cu_seqlens.data_ptr<int64_t>(),
       kv_lens.data_ptr<int64_t>(), slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(),
-      o.data_ptr(), ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, static_cast<int>(B),
+      o.data_ptr(), ws.data_ptr(), ws_bytes, static_cast<int>(B),
       q.size(1), static_cast<int>(q.size(2)), static_cast<int>(k.size(1)),
       static_cast<int>(q.size(3)), static_cast<int>(k.size(2)), k.size(0), block_table.size(0),
-      block_table.stride(0), k.stride(0), k.stride(1), S,
+      block_table.stride(0), k.stride(0), k.stride(1), 0,
       reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
   check_status(st, "gqa_mixed_attention");
   return o;

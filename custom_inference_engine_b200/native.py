@@ -43,8 +43,7 @@ SIGNATURES = {
     "cie_decode_attention_noalloc": (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
                                              c_int, c_int, c_int, c_int, c_int, c_i64, c_i64,
                                              c_i64, c_i64, c_i64, c_int, c_ptr]),
-    "cie_mixed_default_splits": (c_int, [c_int, c_i64, c_int, c_int]),
-    "cie_mixed_workspace_bytes": (c_size, [c_i64, c_int, c_int, c_int]),
+    "cie_mixed_workspace_bytes": (c_size, [c_int, c_i64, c_int, c_int, c_int]),
     "cie_mixed_attention": (c_int, [c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
                                     c_ptr, c_ptr, c_size, c_int, c_i64, c_int, c_int, c_int,
                                     c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_ptr]),

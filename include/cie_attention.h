@@ -123,13 +123,14 @@ int cie_decode_attention_noalloc(const void* q, const void* k, const void* v,
 
 /* ---- varlen mixed (chunked prefill + decode) attention --------------------- */
 
-/* Key-range splits used when cie_mixed_attention() is given num_splits <= 0:
- * 1 unless the tile pairs alone would leave SMs of `device` idle. */
-int cie_mixed_default_splits(int batch, int64_t total_tokens, int num_kv_heads, int device);
-
-/* Bytes of fp32 workspace the split path needs (0 when num_splits == 1). */
-size_t cie_mixed_workspace_bytes(int64_t total_tokens, int num_q_heads, int head_dim,
-                                 int num_splits);
+/* Bytes of device workspace cie_mixed_attention() needs for `batch`
+ * sequences of `total_tokens` rows in all, with the same num_splits, on
+ * `device` (its SM count sizes the automatic plan; -1: 148 SMs). The
+ * workspace holds the work plan (made on the device by the call itself), a
+ * counter per split tile pair and the fp32 partials of split pairs; about
+ * 20 MB on 148 SMs with num_splits <= 0, nothing needs to start at zero. */
+size_t cie_mixed_workspace_bytes(int batch, int64_t total_tokens, int num_kv_heads,
+                                 int num_splits, int device);
 
 /*
  * Causal attention for a batch of chunks in one call.
@@ -141,10 +142,16 @@ size_t cie_mixed_workspace_bytes(int64_t total_tokens, int num_q_heads, int head
  *   of slot slot_ids[b] (the chunk's own K/V are already in the pool).
  *   max_seqlen bounds every chunk length (the bucket's token count).
  *   Rows outside every [cu_seqlens[b], cu_seqlens[b+1]) are not written.
- * num_splits: key ranges per tile pair (<= 0: cie_mixed_default_splits,
- * at most 16); with more than one, partials go to `workspace`
- * (>= cie_mixed_workspace_bytes(...), 16-byte aligned) and a second kernel
- * merges them.
+ * Work partition: a planning kernel (one CTA) lists the (sequence, kv head,
+ * 36-token tile pair) units that exist, cuts long ones into key ranges and
+ * orders the pieces largest first; the attention kernel (launched with
+ * programmatic stream serialization) runs one CTA per piece, and the last
+ * piece of a cut pair to finish merges the fp32 partials of the others.
+ * num_splits <= 0: automatic cut (pieces of at most max(2, ceil(total key
+ * blocks / SMs)) 128-key blocks, <= 16 per pair); num_splits = S in
+ * [1, 16]: every pair is cut into ceil(nb / max(ceil(nb / S), 2)) ranges.
+ * workspace: >= cie_mixed_workspace_bytes(batch, total_tokens, num_kv_heads,
+ * num_splits, device) bytes, 16-byte aligned. batch <= 2048.
  */
 int cie_mixed_attention(const void* q, const void* k, const void* v, int64_t max_seqlen,
                         const int64_t* cu_seqlens, const int64_t* kv_lens,

@@ -85,13 +85,25 @@ def test_mixed_and_update_argument_checks():
     assert mixed(d=128) == -2
     assert mixed(q=None) == -1
     assert mixed(max_seqlen=0) == 0
-    assert mixed(splits=4) == -5                 # split path without workspace
+    for splits in (0, 1, 4):
+        assert mixed(splits=splits) == -5        # the plan always needs workspace
     assert mixed(splits=17) == -1
-    assert lib.cie_mixed_workspace_bytes(2048, 14, 64, 1) == 0
-    assert lib.cie_mixed_workspace_bytes(2048, 14, 64, 3) == 3 * 2048 * 14 * 66 * 4
-    assert lib.cie_mixed_default_splits(4, 2048, 2, -1) == 1
-    assert lib.cie_mixed_default_splits(32, 32, 2, -1) == 2
-    assert lib.cie_mixed_default_splits(1, 1, 2, -1) == 16
+    assert mixed(batch=2049, T=4096, max_seqlen=16) == -2
+
+    def plan_bytes(batch, T, hkv, splits, sms=148):
+        # header | items (2 x int4) | split counters | records of 252 rows x 66 fp32
+        r256 = lambda x: (x + 255) // 256 * 256
+        units = hkv * ((T + 35) // 36 + batch)
+        if splits >= 1:
+            items, split, rec = splits * units, (units if splits > 1 else 0), \
+                (splits * units if splits > 1 else 0)
+        else:
+            items, split, rec = units + sms, sms, 2 * sms
+        return 256 + r256(items * 32) + r256(split * 4) + rec * 252 * 66 * 4
+    for args in ((4, 2048, 2, 1), (4, 2048, 2, 3), (4, 2048, 2, 0), (32, 2048, 2, 0),
+                 (1, 1, 2, 16)):
+        assert lib.cie_mixed_workspace_bytes(*args, -1) == plan_bytes(*args)
+    assert lib.cie_mixed_workspace_bytes(4, 2048, 2, 0, -1) < 24 << 20
     assert lib.cie_kv_mixed_update(None, p, p, p, p, p, 4, 2, 64, 16, 10, 2048, 1024, 1152, 64,
                                    1152, 64, None) == -1
     # fused RoPE + KV write: qkv row 1152, cos/sin row 64, pool strides 2048 / 1024
