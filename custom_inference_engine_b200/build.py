@@ -63,6 +63,17 @@ def build_ops(force: bool = False, verbose: bool = False) -> Path:
     deps = [CSRC / "torch_ops.cpp", INCLUDE / "cie_attention.h", LIB]
     if not force and not _stale(OPS, deps):
         return OPS
+    # torch.utils.cpp_extension.load also loads the library into the calling
+    # process, which would register the inference:: namespace a second time when
+    # the package later loads its in-tree copy: compile in a child process.
+    subprocess.run([sys.executable, "-c",
+                    "import sys; sys.path.insert(0, %r); "
+                    "from custom_inference_engine_b200 import build; "
+                    "build._compile_ops(%r)" % (str(PKG.parent), verbose)], check=True)
+    return OPS
+
+
+def _compile_ops(verbose: bool = False) -> None:
     from torch.utils.cpp_extension import load
     bdir = PKG / "_build"
     bdir.mkdir(exist_ok=True)
@@ -77,7 +88,6 @@ def build_ops(force: bool = False, verbose: bool = False) -> Path:
          verbose=verbose)
     shutil.copy2(bdir / "_cie_torch_ops.so", str(OPS) + ".tmp")
     os.replace(str(OPS) + ".tmp", OPS)
-    return OPS
 
 
 def build_all(force: bool = False, verbose: bool = False) -> None:
