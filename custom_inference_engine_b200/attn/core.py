@@ -152,14 +152,18 @@ class TritonQwen2Attention(torch.nn.Module):
                 kv_manager.decode_update(layer, metadata.slot_ids, k, v)
             else:
                 kv_manager.mixed_update(layer, metadata.pages, metadata.offsets, k, v)
+        lens = getattr(metadata, "attn_lens", None)
         if metadata.full_decode:
+            if lens is None:
+                lens = kv_manager.lens[metadata.slot_ids] + 1
             o = gqa_decode_attention_op(q, kv_manager.keys[layer], kv_manager.values[layer],
-                                        kv_manager.lens[metadata.slot_ids] + 1,
-                                        slot_ids=metadata.slot_ids,
+                                        lens, slot_ids=metadata.slot_ids,
                                         block_table=kv_manager.block_table)
         else:
+            if lens is None:
+                lens = kv_manager.lens[metadata.slot_ids]
             o = gqa_mixed_attention_op(q, kv_manager.keys[layer], kv_manager.values[layer],
-                                       kv_lens=kv_manager.lens[metadata.slot_ids],
+                                       kv_lens=lens,
                                        max_seqlen=metadata.max_seqlen,
                                        cu_seqlens=metadata.cu_seqlens,
                                        slot_ids=metadata.slot_ids,

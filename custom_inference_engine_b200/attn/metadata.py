@@ -25,6 +25,10 @@ class AttentionMetadata:
         self.offsets = torch.zeros((token_count,), dtype=torch.long, device=device)
         self.max_seqlen = token_count
         self.full_decode = full_decode
+        # Optional, not in the reference: the attention lengths of this pass
+        # (decode: lens[slot_ids] + 1, mixed: lens[slot_ids]) computed once by
+        # the caller; when None every layer computes them from the KV storage.
+        self.attn_lens = None
 
     def prepare_full_graph(self, batch_size: int):
         """Fixed-size slot / cu_seqlens buffers for a captured CUDA graph."""

@@ -1,8 +1,9 @@
 """Builds the two native libraries of the package, in-tree, for sm_100a.
 
 * ``libcie_attention.so`` -- the CUDA kernels and their C ABI
-  (``include/cie_attention.h``), compiled by nvcc from ``csrc/cie_unity.cu``;
-  the CUDA runtime is linked statically and its symbols are not exported.
+  (``include/cie_attention.h``, ``include/cie_model_ops.h``), compiled by nvcc
+  from ``csrc/cie_unity.cu`` and ``csrc/model_ops.cu``; the CUDA runtime is
+  linked statically and its symbols are not exported.
 * ``_cie_torch_ops.so`` -- the ``inference::*`` torch ops
   (``csrc/torch_ops.cpp``) linked against the library above
   (rpath ``$ORIGIN``), built with ``torch.utils.cpp_extension``.
@@ -45,22 +46,36 @@ def _cu_deps():
 
 
 def build_lib(force: bool = False, verbose: bool = False) -> Path:
+    """Two objects linked into one library: the attention kernels
+    (``cie_unity.cu``, --use_fast_math) and the Qwen2 body kernels
+    (``model_ops.cu``, IEEE division and library expf / rsqrtf, so that they
+    round like torch's own kernels)."""
     if not force and not _stale(LIB, _cu_deps()):
         return LIB
-    cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--use_fast_math",
-           "-Xcompiler", "-fPIC,-O3", "-shared", "-I", str(INCLUDE), "-I", str(CSRC),
-           "-Xlinker", "--exclude-libs,ALL", "-o", str(LIB) + ".tmp",
-           str(CSRC / "cie_unity.cu")]
+    bdir = PKG / "_build"
+    bdir.mkdir(exist_ok=True)
+    common = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3",
+              "-I", str(INCLUDE), "-I", str(CSRC)]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd))
+        common.insert(1, "-Xptxas=-v")
+    objs = [(CSRC / "cie_unity.cu", ["--use_fast_math"]), (CSRC / "model_ops.cu", [])]
+    out = []
+    for src, extra in objs:
+        obj = bdir / (src.stem + ".o")
+        cmd = [*common, *extra, "-c", "-o", str(obj), str(src)]
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+        out.append(str(obj))
+    cmd = [_nvcc(), *ARCH, "-shared", "-Xlinker", "--exclude-libs,ALL", "-o", str(LIB) + ".tmp",
+           *out]
     subprocess.run(cmd, check=True)
     os.replace(str(LIB) + ".tmp", LIB)
     return LIB
 
 
 def build_ops(force: bool = False, verbose: bool = False) -> Path:
-    deps = [CSRC / "torch_ops.cpp", INCLUDE / "cie_attention.h", LIB]
+    deps = [CSRC / "torch_ops.cpp", *sorted(INCLUDE.glob("*.h")), LIB]
     if not force and not _stale(OPS, deps):
         return OPS
     # torch.utils.cpp_extension.load also loads the library into the calling

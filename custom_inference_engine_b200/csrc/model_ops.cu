@@ -1,0 +1,183 @@
+// Element-wise kernels of the Qwen2 decoder body that surround the attention
+// path: RMSNorm, residual add + RMSNorm, and SiLU(gate) * up.
+//
+// In the reference engine these are Hugging Face Qwen2 modules
+// (Qwen2RMSNorm, the decoder layer's residual adds, Qwen2MLP's act_fn(gate) *
+// up) that torch.compile fuses into a few generated kernels; eagerly they
+// are about 20 launches per layer. Here each is one launch. They follow
+// torch's fp16 recipe operation for operation so the results match HF's
+// modules: fp16 + fp16 residual adds rounded once; RMSNorm in fp32
+// (sum of squares, times 1/hidden, + eps, rsqrt, scale), rounded to fp16,
+// then multiplied by the fp16 weight and rounded again; SiLU in fp32 as
+// x / (1 + exp(-x)), rounded to fp16, times up, rounded again. Only the order
+// of the sum of squares differs from torch's reduction.
+//
+// This file is compiled WITHOUT --use_fast_math (expf, the division and
+// rsqrtf keep their IEEE / library accuracy), separately from the attention
+// kernels.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "cie_host.h"
+#include "cie_model_ops.h"
+
+namespace cie {
+namespace body {
+
+constexpr int kWarpsPerCta = 4;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// One warp per row; 8 halves (16 bytes) per lane per step. With `delta`,
+// h = h + delta is written back to h first (the residual stream).
+template <bool kAdd>
+__global__ void __launch_bounds__(32 * kWarpsPerCta)
+    rms_norm_kernel(__half* __restrict__ h, const __half* __restrict__ delta,
+                    const __half* __restrict__ w, __half* __restrict__ out, int64_t rows,
+                    int hidden, int64_t h_stride, int64_t d_stride, int64_t o_stride,
+                    float eps) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  __half* hr = h + row * h_stride;
+  const int chunks = hidden >> 3;
+  float ss = 0.f;
+  for (int c = lane; c < chunks; c += 32) {
+    uint4 x = reinterpret_cast<const uint4*>(hr)[c];
+    if (kAdd) {
+      const uint4 d = reinterpret_cast<const uint4*>(delta + row * d_stride)[c];
+      __half2* xh = reinterpret_cast<__half2*>(&x);
+      const __half2* dh = reinterpret_cast<const __half2*>(&d);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) xh[i] = __hadd2_rn(xh[i], dh[i]);
+      reinterpret_cast<uint4*>(hr)[c] = x;
+    }
+    const __half2* xh = reinterpret_cast<const __half2*>(&x);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(xh[i]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss * (1.0f / static_cast<float>(hidden)) + eps);
+  __half* orow = out + row * o_stride;
+  for (int c = lane; c < chunks; c += 32) {
+    // this lane wrote chunk c of h above: its own store is visible to it
+    const uint4 x = reinterpret_cast<const uint4*>(hr)[c];
+    const uint4 wv = reinterpret_cast<const uint4*>(w)[c];
+    const __half2* xh = reinterpret_cast<const __half2*>(&x);
+    const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+    uint4 y;
+    __half2* yh = reinterpret_cast<__half2*>(&y);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(xh[i]);
+      const __half2 n = __floats2half2_rn(f.x * r, f.y * r);
+      yh[i] = __hmul2_rn(wh[i], n);
+    }
+    reinterpret_cast<uint4*>(orow)[c] = y;
+  }
+}
+
+// out[r, i] = half(silu(gate[r, i])) * up[r, i], 8 elements per thread.
+__global__ void silu_mul_kernel(const __half* __restrict__ gate, const __half* __restrict__ up,
+                                __half* __restrict__ out, int64_t rows, int inter,
+                                int64_t g_stride, int64_t u_stride, int64_t o_stride) {
+  const int chunks = inter >> 3;
+  const int64_t total = rows * chunks;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = e / chunks;
+    const int c = static_cast<int>(e - r * chunks);
+    const uint4 g = reinterpret_cast<const uint4*>(gate + r * g_stride)[c];
+    const uint4 u = reinterpret_cast<const uint4*>(up + r * u_stride)[c];
+    const __half2* gh = reinterpret_cast<const __half2*>(&g);
+    const __half2* uh = reinterpret_cast<const __half2*>(&u);
+    uint4 y;
+    __half2* yh = reinterpret_cast<__half2*>(&y);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = __half22float2(gh[i]);
+      const __half2 s = __floats2half2_rn(x.x / (1.0f + expf(-x.x)), x.y / (1.0f + expf(-x.y)));
+      yh[i] = __hmul2_rn(s, uh[i]);
+    }
+    reinterpret_cast<uint4*>(out + r * o_stride)[c] = y;
+  }
+}
+
+inline bool aligned_rows(const void* p, int64_t stride) {
+  return aligned16(p) && (stride % 8) == 0;
+}
+
+}  // namespace body
+}  // namespace cie
+
+extern "C" {
+
+int cie_rms_norm(void* h, const void* delta, const void* weight, void* out, int64_t rows,
+                 int hidden, int64_t h_stride, int64_t delta_stride, int64_t out_stride,
+                 float eps, cie_stream_t stream) {
+  using namespace cie;
+  using namespace cie::body;
+  if (rows < 0 || hidden < 0) return fail(CIE_ERR_INVALID_ARGUMENT, "negative rows / hidden");
+  if (rows == 0 || hidden == 0) return CIE_OK;
+  if (!h || !weight || !out) return fail(CIE_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (hidden % 8) return fail(CIE_ERR_UNSUPPORTED, "hidden %d must be a multiple of 8", hidden);
+  if (!aligned_rows(h, h_stride) || !aligned_rows(out, out_stride) || !aligned16(weight) ||
+      (delta && !aligned_rows(delta, delta_stride)))
+    return fail(CIE_ERR_ALIGNMENT, "rows must start on 16-byte boundaries");
+  if (h_stride < hidden || out_stride < hidden || (delta && delta_stride < hidden))
+    return fail(CIE_ERR_INVALID_ARGUMENT, "row strides must be >= hidden");
+  if (!(eps >= 0.f)) return fail(CIE_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+  const int64_t ctas = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
+  if (ctas > 0x7fffffff) return fail(CIE_ERR_OVERFLOW, "too many rows");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto* hp = static_cast<__half*>(h);
+  auto* op = static_cast<__half*>(out);
+  const auto* wp = static_cast<const __half*>(weight);
+  if (delta)
+    rms_norm_kernel<true><<<static_cast<unsigned>(ctas), 32 * kWarpsPerCta, 0, s>>>(
+        hp, static_cast<const __half*>(delta), wp, op, rows, hidden, h_stride, delta_stride,
+        out_stride, eps);
+  else
+    rms_norm_kernel<false><<<static_cast<unsigned>(ctas), 32 * kWarpsPerCta, 0, s>>>(
+        hp, nullptr, wp, op, rows, hidden, h_stride, 0, out_stride, eps);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "rms_norm launch: %s", cudaGetErrorString(e));
+  return CIE_OK;
+}
+
+int cie_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int inter,
+                 int64_t gate_stride, int64_t up_stride, int64_t out_stride,
+                 cie_stream_t stream) {
+  using namespace cie;
+  using namespace cie::body;
+  if (rows < 0 || inter < 0) return fail(CIE_ERR_INVALID_ARGUMENT, "negative rows / size");
+  if (rows == 0 || inter == 0) return CIE_OK;
+  if (!gate || !up || !out) return fail(CIE_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (inter % 8) return fail(CIE_ERR_UNSUPPORTED, "size %d must be a multiple of 8", inter);
+  if (!aligned_rows(gate, gate_stride) || !aligned_rows(up, up_stride) ||
+      !aligned_rows(out, out_stride))
+    return fail(CIE_ERR_ALIGNMENT, "rows must start on 16-byte boundaries");
+  if (gate_stride < inter || up_stride < inter || out_stride < inter)
+    return fail(CIE_ERR_INVALID_ARGUMENT, "row strides must be >= size");
+  const int64_t total = rows * (inter / 8);
+  const int threads = 256;
+  const int64_t want = (total + threads - 1) / threads;
+  const unsigned blocks = static_cast<unsigned>(want < 8L * sm_count() ? want : 8L * sm_count());
+  silu_mul_kernel<<<blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(gate), static_cast<const __half*>(up), static_cast<__half*>(out),
+      rows, inter, gate_stride, up_stride, out_stride);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "silu_mul launch: %s", cudaGetErrorString(e));
+  return CIE_OK;
+}
+
+}  // extern "C"

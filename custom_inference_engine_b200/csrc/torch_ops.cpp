@@ -12,7 +12,11 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <algorithm>
+#include <vector>
+
 #include "cie_attention.h"
+#include "cie_model_ops.h"
 
 namespace {
 
@@ -267,6 +271,71 @@ at::Tensor rope_kv_mixed_update(const at::Tensor& qkv, const at::Tensor& cos,
   return q;
 }
 
+// ---- Qwen2 body helpers (cie_model_ops.h) ----------------------------------
+
+void check_rows(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kHalf, name, " must be a float16 CUDA tensor");
+  TORCH_CHECK(t.dim() >= 1 && t.stride(-1) == 1, name, " must have a unit inner stride");
+  for (int64_t d = 0; d + 2 < t.dim(); ++d)
+    TORCH_CHECK(t.size(d) == 1 || t.stride(d) == t.stride(d + 1) * t.size(d + 1), name,
+                " must be contiguous apart from its row stride");
+}
+
+int64_t row_stride(const at::Tensor& t) { return t.dim() >= 2 ? t.stride(-2) : t.size(-1); }
+
+at::Tensor rms_norm(const at::Tensor& x, const at::Tensor& weight, double eps) {
+  check_rows(x, "x");
+  TORCH_CHECK(weight.is_cuda() && weight.scalar_type() == at::kHalf && weight.dim() == 1 &&
+                  weight.is_contiguous() && weight.size(0) == x.size(-1),
+              "weight must be a contiguous float16 (hidden,) CUDA tensor");
+  c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor out = at::empty(x.sizes(), x.options());
+  const int64_t rows = x.numel() / std::max<int64_t>(x.size(-1), 1);
+  const int st = cie_rms_norm(const_cast<void*>(x.data_ptr()), nullptr, weight.data_ptr(),
+                              out.data_ptr(), rows, static_cast<int>(x.size(-1)), row_stride(x), 0,
+                              x.size(-1), static_cast<float>(eps),
+                              reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "rms_norm");
+  return out;
+}
+
+at::Tensor add_rms_norm(at::Tensor& residual, const at::Tensor& delta, const at::Tensor& weight,
+                        double eps) {
+  check_rows(residual, "residual");
+  check_rows(delta, "delta");
+  TORCH_CHECK(residual.sizes() == delta.sizes(), "residual and delta shapes differ");
+  TORCH_CHECK(weight.is_cuda() && weight.scalar_type() == at::kHalf && weight.dim() == 1 &&
+                  weight.is_contiguous() && weight.size(0) == residual.size(-1),
+              "weight must be a contiguous float16 (hidden,) CUDA tensor");
+  c10::cuda::CUDAGuard guard(residual.device());
+  at::Tensor out = at::empty(residual.sizes(), residual.options());
+  const int64_t rows = residual.numel() / std::max<int64_t>(residual.size(-1), 1);
+  const int st = cie_rms_norm(residual.data_ptr(), delta.data_ptr(), weight.data_ptr(),
+                              out.data_ptr(), rows, static_cast<int>(residual.size(-1)),
+                              row_stride(residual), row_stride(delta), residual.size(-1),
+                              static_cast<float>(eps),
+                              reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "add_rms_norm");
+  return out;
+}
+
+at::Tensor silu_and_mul(const at::Tensor& gate_up) {
+  check_rows(gate_up, "gate_up");
+  TORCH_CHECK(gate_up.size(-1) % 2 == 0, "gate_up must hold [gate | up]");
+  c10::cuda::CUDAGuard guard(gate_up.device());
+  const int64_t n = gate_up.size(-1) / 2;
+  std::vector<int64_t> shape(gate_up.sizes().begin(), gate_up.sizes().end());
+  shape.back() = n;
+  at::Tensor out = at::empty(shape, gate_up.options());
+  const int64_t rows = gate_up.numel() / std::max<int64_t>(gate_up.size(-1), 1);
+  const auto* g = static_cast<const at::Half*>(gate_up.data_ptr());
+  const int st = cie_silu_mul(g, g + n, out.data_ptr(), rows, static_cast<int>(n),
+                              row_stride(gate_up), row_stride(gate_up), n,
+                              reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "silu_and_mul");
+  return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(inference, m) {
@@ -291,6 +360,9 @@ TORCH_LIBRARY(inference, m) {
   m.def(
       "rope_kv_mixed_update(Tensor qkv, Tensor cos, Tensor sin, Tensor(a!) k_cache, "
       "Tensor(b!) v_cache, Tensor pages, Tensor offsets) -> Tensor");
+  m.def("rms_norm(Tensor x, Tensor weight, float eps) -> Tensor");
+  m.def("add_rms_norm(Tensor(a!) residual, Tensor delta, Tensor weight, float eps) -> Tensor");
+  m.def("silu_and_mul(Tensor gate_up) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(inference, CUDA, m) {
@@ -301,4 +373,7 @@ TORCH_LIBRARY_IMPL(inference, CUDA, m) {
   m.impl("kv_mixed_update", &kv_mixed_update);
   m.impl("rope_kv_decode_update", &rope_kv_decode_update);
   m.impl("rope_kv_mixed_update", &rope_kv_mixed_update);
+  m.impl("rms_norm", &rms_norm);
+  m.impl("add_rms_norm", &add_rms_norm);
+  m.impl("silu_and_mul", &silu_and_mul);
 }

@@ -11,6 +11,10 @@ decode steps go through ``inference::gqa_decode_attention`` and can be captured
 in one CUDA graph per batch (embedding, 24 layers, lm_head, argmax and the
 slot-length advance).
 
+By default the decoder body around the attention runs through
+``FusedQwen2Body`` (RMSNorm, residual adds and SiLU-mul as CUDA kernels of this
+package, about 10 launches per layer); ``fused_body=False`` runs HF's modules.
+
 This is the harness that measures Qwen2.5-0.5B-shape tokens/s and checks greedy
 tokens against HF's own attention. It is not a serving scheduler: there is no
 request queue, admission control or preemption; every slot gets enough pages up
@@ -53,6 +57,60 @@ def random_qwen2(config, seed: int = 0, device="cuda", dtype=torch.float16):
     return model.to(dtype).eval()
 
 
+class FusedQwen2Body:
+    """The Qwen2 decoder stack of ``model`` with its element-wise work in CUDA
+    kernels of this package: ``inference::rms_norm`` for the first input norm,
+    ``inference::add_rms_norm`` for every residual add and the norm after it
+    (post-attention norm, next layer's input norm, final norm),
+    ``inference::silu_and_mul`` for SiLU(gate) * up after ONE projection GEMM
+    over the concatenated gate and up weights, and a rotary table indexed by
+    position instead of recomputing cos / sin per pass. The attention modules
+    (``TritonQwen2Attention``) and the projections are the model's own.
+
+    It computes what HF's ``Qwen2Model.forward`` computes (same operations and
+    fp16 roundings; the sum of squares of RMSNorm and the gate / up GEMM may
+    accumulate in another order) in about 10 launches per layer instead of
+    about 27.
+    """
+
+    def __init__(self, model, max_positions: int):
+        from .attn import core  # noqa: F401  (loads the torch ops)
+
+        m = model.model
+        self.model = model
+        self.embed = m.embed_tokens
+        self.layers = list(m.layers)
+        self.eps = float(model.config.rms_norm_eps)
+        self.in_w = [layer.input_layernorm.weight for layer in self.layers]
+        self.post_w = [layer.post_attention_layernorm.weight for layer in self.layers]
+        self.next_w = self.in_w[1:] + [m.norm.weight]
+        with torch.no_grad():
+            self.gate_up = [torch.cat([layer.mlp.gate_proj.weight, layer.mlp.up_proj.weight])
+                            for layer in self.layers]
+            dev = self.embed.weight.device
+            pos = torch.arange(max_positions, device=dev).view(1, -1)
+            probe = torch.zeros(1, 1, dtype=self.embed.weight.dtype, device=dev)
+            cos, sin = m.rotary_emb(probe, pos)
+        self.cos, self.sin = cos[0].contiguous(), sin[0].contiguous()  # (positions, head_dim)
+        for layer in self.layers:
+            if layer.mlp.gate_proj.bias is not None or layer.mlp.up_proj.bias is not None:
+                raise ValueError("Qwen2 MLP projections carry no bias")
+
+    def __call__(self, input_ids, position_ids, kv, metadata):
+        ops = torch.ops.inference
+        h = self.embed(input_ids)
+        pos = position_ids.view(-1)
+        cos = self.cos.index_select(0, pos).unsqueeze(0)
+        sin = self.sin.index_select(0, pos).unsqueeze(0)
+        x = ops.rms_norm(h, self.in_w[0], self.eps)
+        for i, layer in enumerate(self.layers):
+            a, _ = layer.self_attn(x, (cos, sin), kv_manager=kv, metadata=metadata)
+            x = ops.add_rms_norm(h, a, self.post_w[i], self.eps)
+            y = ops.silu_and_mul(torch.nn.functional.linear(x, self.gate_up[i]))
+            x = ops.add_rms_norm(h, layer.mlp.down_proj(y), self.next_w[i], self.eps)
+        return x
+
+
 @dataclass
 class PrefillResult:
     first_tokens: list          # greedy token after each prompt
@@ -69,7 +127,7 @@ class PagedRunner:
     """
 
     def __init__(self, model, max_cache_len: int, n_slots: int, page_seed: int = 0,
-                 token_budget: int = 2048):
+                 token_budget: int = 2048, fused_body: bool = True):
         from .attn.core import use_cuda_attention
         from .kv_cache.storage import KVStorage
 
@@ -83,6 +141,9 @@ class PagedRunner:
         self.free_pages = (torch.randperm(self.kv.n_pages - 1, generator=g) + 1).tolist()
         self.token_budget = token_budget
         self.host_lens = [0] * n_slots  # host mirror of kv.lens
+        # fused_body: the CUDA element-wise kernels around the attention
+        # (FusedQwen2Body); False runs HF's Qwen2Model modules as they are
+        self.body = FusedQwen2Body(model, max_cache_len) if fused_body else None
 
     # ---- slots -------------------------------------------------------------
     def admit(self, slot: int, capacity_tokens: int) -> None:
@@ -100,6 +161,11 @@ class PagedRunner:
 
     # ---- forward -----------------------------------------------------------
     def _hidden(self, input_ids, position_ids, metadata):
+        # the attention lengths of this pass, once for all layers
+        lens = self.kv.lens[metadata.slot_ids]
+        metadata.attn_lens = lens + 1 if metadata.full_decode else lens
+        if self.body is not None:
+            return self.body(input_ids, position_ids, self.kv, metadata)
         out = self.model.model(input_ids=input_ids, position_ids=position_ids,
                                attention_mask={"full_attention": None}, kv_manager=self.kv,
                                metadata=metadata, use_cache=False)

@@ -29,7 +29,7 @@ c_int = ctypes.c_int
 c_ptr = ctypes.c_void_p
 c_size = ctypes.c_size_t
 
-# name -> (restype, argtypes); mirrors include/cie_attention.h
+# name -> (restype, argtypes); mirrors include/cie_attention.h and include/cie_model_ops.h
 SIGNATURES = {
     "cie_version": (c_int, []),
     "cie_status_string": (ctypes.c_char_p, [c_int]),
@@ -59,6 +59,10 @@ SIGNATURES = {
     "cie_rope_kv_mixed_update": (c_int, [c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr,
                                          c_ptr, c_ptr, c_i64, c_int, c_int, c_int, c_int, c_i64,
                                          c_i64, c_i64, c_ptr]),
+    # include/cie_model_ops.h
+    "cie_rms_norm": (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_int, c_i64, c_i64, c_i64,
+                             ctypes.c_float, c_ptr]),
+    "cie_silu_mul": (c_int, [c_ptr, c_ptr, c_ptr, c_i64, c_int, c_i64, c_i64, c_i64, c_ptr]),
 }
 
 CIE_OK = 0
@@ -156,6 +160,18 @@ def _register_fakes() -> None:
     @torch.library.register_fake("inference::rope_kv_mixed_update")
     def _rope_mix_fake(qkv, cos, sin, k_cache, v_cache, pages, offsets):
         return _rope_out(qkv, k_cache)
+
+    @torch.library.register_fake("inference::rms_norm")
+    def _rms_fake(x, weight, eps):
+        return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+    @torch.library.register_fake("inference::add_rms_norm")
+    def _add_rms_fake(residual, delta, weight, eps):
+        return torch.empty_like(residual, memory_format=torch.contiguous_format)
+
+    @torch.library.register_fake("inference::silu_and_mul")
+    def _silu_mul_fake(gate_up):
+        return gate_up.new_empty((*gate_up.shape[:-1], gate_up.shape[-1] // 2))
 
 
 def stream_ptr(stream=None) -> int:

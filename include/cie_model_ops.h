@@ -1,0 +1,52 @@
+/*
+ * cie_model_ops.h -- element-wise kernels of the Qwen2 decoder body around
+ * the attention path, in libcie_attention.so (same conventions and status
+ * codes as cie_attention.h: device pointers, element strides, asynchronous on
+ * `stream`, no allocation, no host synchronisation, graph-capturable).
+ *
+ * These have no counterpart in the reference's attention FFI: the reference
+ * runs Hugging Face's Qwen2 modules (Qwen2RMSNorm, the decoder layer's
+ * residual adds, Qwen2MLP) and leaves their fusion to torch.compile. The
+ * model runner of this package calls them instead of those modules. They
+ * follow torch's fp16 arithmetic step for step (fp32 inside, the same
+ * roundings to fp16); only the order of RMSNorm's sum of squares differs.
+ */
+#ifndef CIE_MODEL_OPS_H_
+#define CIE_MODEL_OPS_H_
+
+#include <stdint.h>
+
+#include "cie_attention.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/*
+ * RMSNorm of `rows` rows of `hidden` fp16 values, Qwen2RMSNorm's arithmetic:
+ *   out = weight * fp16(x * rsqrt(mean(x^2) + eps))      (fp32 inside)
+ * With delta == NULL, x = h (read only). With delta != NULL the residual add
+ * comes first and is written back: h = fp16(h + delta), x = the new h (the
+ * decoder layer's `residual + hidden_states` followed by the next norm).
+ * Row strides in elements; every row 16-byte aligned; hidden % 8 == 0.
+ */
+int cie_rms_norm(void* h, const void* delta, const void* weight, void* out, int64_t rows,
+                 int hidden, int64_t h_stride, int64_t delta_stride, int64_t out_stride,
+                 float eps, cie_stream_t stream);
+
+/*
+ * Qwen2MLP's act_fn(gate) * up with act_fn = SiLU:
+ *   out = fp16(fp16(g / (1 + exp(-g))) * up)             (fp32 inside)
+ * gate / up / out: `rows` rows of `size` fp16 values at the given row
+ * strides (gate and up may be the two halves of one fused projection).
+ * Every row 16-byte aligned; size % 8 == 0.
+ */
+int cie_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int size,
+                 int64_t gate_stride, int64_t up_stride, int64_t out_stride,
+                 cie_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CIE_MODEL_OPS_H_ */

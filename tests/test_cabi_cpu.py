@@ -8,19 +8,22 @@ import pytest
 
 from custom_inference_engine_b200 import native
 
-HEADER = Path(__file__).resolve().parents[1] / "include" / "cie_attention.h"
+HEADERS = sorted((Path(__file__).resolve().parents[1] / "include").glob("*.h"))
 
 
 def declared_functions():
-    text = HEADER.read_text()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(cie_[a-z_0-9]+)\s*\(", text)))
+    names = set()
+    for header in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(cie_[a-z_0-9]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_header_declares_the_expected_entry_points():
     names = declared_functions()
     for must in ("cie_decode_attention", "cie_mixed_attention", "cie_kv_decode_update",
-                 "cie_kv_mixed_update", "cie_decode_workspace_bytes"):
+                 "cie_kv_mixed_update", "cie_decode_workspace_bytes", "cie_rms_norm",
+                 "cie_silu_mul"):
         assert must in names
 
 
@@ -121,3 +124,27 @@ def test_mixed_and_update_argument_checks():
                                          16, 10, 3, 10, 2048, 1024, None) == -1
     assert lib.cie_kv_decode_update(p, p, p, p, p, p, p, 4, 2, 64, 16, 10, 3, 10, 100, 1024,
                                     1152, 64, 1152, 64, None) == -1
+
+
+def test_body_kernel_argument_checks():
+    """RMSNorm / SiLU-mul entry points reject bad arguments on the host."""
+    lib = native.lib()
+    p = 1 << 20
+    rms = lambda h=p, d=None, w=p, o=p, rows=4, hidden=896, hs=896, ds=896, os_=896, eps=1e-6: \
+        lib.cie_rms_norm(h, d, w, o, rows, hidden, hs, ds, os_, eps, None)
+    assert rms(rows=0) == 0
+    assert rms(h=None) == -1
+    assert rms(rows=-1) == -1
+    assert rms(hidden=900, hs=900, os_=900) == -2
+    assert rms(h=p + 2) == -4
+    assert rms(hs=900) == -4
+    assert rms(d=p + 8) == -4
+    assert rms(hs=888) == -1
+    assert rms(eps=-1.0) == -1
+    silu = lambda g=p, u=p + 9728, o=p, rows=4, n=4864, gs=9728, us=9728, os_=4864: \
+        lib.cie_silu_mul(g, u, o, rows, n, gs, us, os_, None)
+    assert silu(rows=0) == 0
+    assert silu(g=None) == -1
+    assert silu(n=4860, os_=4860) == -2
+    assert silu(u=p + 2) == -4
+    assert silu(os_=4800) == -1

@@ -7,7 +7,8 @@ sequence, recomputed every step) -- the reference engine's end-to-end contract
 Prompts are prefilled in mixed passes of at most 64 tokens, so a long prompt
 spans several passes and later passes attend to K/V written by earlier ones;
 the decode steps go through the decode op, eagerly and from a captured CUDA
-graph.
+graph. The runner's default decoder body is FusedQwen2Body (this package's
+RMSNorm / residual / SiLU-mul kernels); HF's own modules are compared too.
 """
 import numpy as np
 import pytest
@@ -43,8 +44,9 @@ def _hf_greedy(model, prompt, n_new):
     return seq[len(prompt):], first_logits
 
 
-def _ours(model, prompts, capture):
-    runner = MR.PagedRunner(model, max_cache_len=4096, n_slots=8, token_budget=64)
+def _ours(model, prompts, capture, fused_body=True):
+    runner = MR.PagedRunner(model, max_cache_len=4096, n_slots=8, token_budget=64,
+                            fused_body=fused_body)
     slots = list(range(1, len(prompts) + 1))
     for s, p in zip(slots, prompts):
         runner.admit(s, len(p) + N_NEW + 4)
@@ -90,3 +92,17 @@ def test_graph_decode_matches_eager(cuda_device):
     eager, _ = _ours(model, prompts, capture=False)
     graphed, _ = _ours(model, prompts, capture=True)
     assert graphed == eager
+
+
+def test_fused_body_matches_hf_body(cuda_device):
+    """The decoder body on this package's RMSNorm / residual / SiLU-mul kernels
+    (FusedQwen2Body) gives the greedy tokens of HF's own modules around the
+    same attention ops, eagerly and captured, with logits within fp16 noise."""
+    model = _model(cuda_device)
+    prompts = _prompts()
+    hf_body, pre_h = _ours(model, prompts, capture=False, fused_body=False)
+    fused, pre_f = _ours(model, prompts, capture=False, fused_body=True)
+    graphed, _ = _ours(model, prompts, capture=True, fused_body=True)
+    assert (pre_f.last_logits - pre_h.last_logits).abs().max().item() <= LOGIT_TOL
+    assert fused == hf_body
+    assert graphed == hf_body
