@@ -33,9 +33,13 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// One warp per row; 8 halves (16 bytes) per lane per step. With `delta`,
+// One warp per row; 8 halves (16 bytes) per lane per chunk. With `delta`,
 // h = h + delta is written back to h first (the residual stream).
-template <bool kAdd>
+// kChunks > 0: the row is held in registers (chunk c of lane l is
+// l + 32 i, i < kChunks, so hidden <= 256 kChunks) and every load of h, delta
+// and the weight is issued before the first use: one memory round trip per
+// row. kChunks == 0: any width, the row is read twice.
+template <bool kAdd, int kChunks>
 __global__ void __launch_bounds__(32 * kWarpsPerCta)
     rms_norm_kernel(__half* __restrict__ h, const __half* __restrict__ delta,
                     const __half* __restrict__ w, __half* __restrict__ out, int64_t rows,
@@ -45,44 +49,95 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta)
   if (row >= rows) return;
   const int lane = threadIdx.x & 31;
   __half* hr = h + row * h_stride;
-  const int chunks = hidden >> 3;
-  float ss = 0.f;
-  for (int c = lane; c < chunks; c += 32) {
-    uint4 x = reinterpret_cast<const uint4*>(hr)[c];
-    if (kAdd) {
-      const uint4 d = reinterpret_cast<const uint4*>(delta + row * d_stride)[c];
-      __half2* xh = reinterpret_cast<__half2*>(&x);
-      const __half2* dh = reinterpret_cast<const __half2*>(&d);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) xh[i] = __hadd2_rn(xh[i], dh[i]);
-      reinterpret_cast<uint4*>(hr)[c] = x;
-    }
-    const __half2* xh = reinterpret_cast<const __half2*>(&x);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __half22float2(xh[i]);
-      ss = fmaf(f.x, f.x, ss);
-      ss = fmaf(f.y, f.y, ss);
-    }
-  }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss * (1.0f / static_cast<float>(hidden)) + eps);
+  const __half* dr = kAdd ? delta + row * d_stride : nullptr;
   __half* orow = out + row * o_stride;
-  for (int c = lane; c < chunks; c += 32) {
-    // this lane wrote chunk c of h above: its own store is visible to it
-    const uint4 x = reinterpret_cast<const uint4*>(hr)[c];
-    const uint4 wv = reinterpret_cast<const uint4*>(w)[c];
-    const __half2* xh = reinterpret_cast<const __half2*>(&x);
-    const __half2* wh = reinterpret_cast<const __half2*>(&wv);
-    uint4 y;
-    __half2* yh = reinterpret_cast<__half2*>(&y);
+  const int chunks = hidden >> 3;
+  const float inv_n = 1.0f / static_cast<float>(hidden);
+  if constexpr (kChunks > 0) {
+    uint4 x[kChunks], d[kChunks], wv[kChunks];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __half22float2(xh[i]);
-      const __half2 n = __floats2half2_rn(f.x * r, f.y * r);
-      yh[i] = __hmul2_rn(wh[i], n);
+    for (int i = 0; i < kChunks; ++i) {
+      const int c = lane + 32 * i;
+      if (c < chunks) {
+        x[i] = reinterpret_cast<const uint4*>(hr)[c];
+        if (kAdd) d[i] = reinterpret_cast<const uint4*>(dr)[c];
+        wv[i] = reinterpret_cast<const uint4*>(w)[c];
+      }
     }
-    reinterpret_cast<uint4*>(orow)[c] = y;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+      const int c = lane + 32 * i;
+      if (c < chunks) {
+        __half2* xh = reinterpret_cast<__half2*>(&x[i]);
+        if (kAdd) {
+          const __half2* dh = reinterpret_cast<const __half2*>(&d[i]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) xh[k] = __hadd2_rn(xh[k], dh[k]);
+          reinterpret_cast<uint4*>(hr)[c] = x[i];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(xh[k]);
+          ss = fmaf(f.x, f.x, ss);
+          ss = fmaf(f.y, f.y, ss);
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss * inv_n + eps);
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+      const int c = lane + 32 * i;
+      if (c < chunks) {
+        const __half2* xh = reinterpret_cast<const __half2*>(&x[i]);
+        const __half2* wh = reinterpret_cast<const __half2*>(&wv[i]);
+        uint4 y;
+        __half2* yh = reinterpret_cast<__half2*>(&y);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(xh[k]);
+          yh[k] = __hmul2_rn(wh[k], __floats2half2_rn(f.x * r, f.y * r));
+        }
+        reinterpret_cast<uint4*>(orow)[c] = y;
+      }
+    }
+  } else {
+    float ss = 0.f;
+    for (int c = lane; c < chunks; c += 32) {
+      uint4 x = reinterpret_cast<const uint4*>(hr)[c];
+      __half2* xh = reinterpret_cast<__half2*>(&x);
+      if (kAdd) {
+        const uint4 d = reinterpret_cast<const uint4*>(dr)[c];
+        const __half2* dh = reinterpret_cast<const __half2*>(&d);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xh[k] = __hadd2_rn(xh[k], dh[k]);
+        reinterpret_cast<uint4*>(hr)[c] = x;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(xh[k]);
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss * inv_n + eps);
+    for (int c = lane; c < chunks; c += 32) {
+      // this lane wrote chunk c of h above: its own store is visible to it
+      const uint4 x = reinterpret_cast<const uint4*>(hr)[c];
+      const uint4 wv = reinterpret_cast<const uint4*>(w)[c];
+      const __half2* xh = reinterpret_cast<const __half2*>(&x);
+      const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+      uint4 y;
+      __half2* yh = reinterpret_cast<__half2*>(&y);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(xh[k]);
+        yh[k] = __hmul2_rn(wh[k], __floats2half2_rn(f.x * r, f.y * r));
+      }
+      reinterpret_cast<uint4*>(orow)[c] = y;
+    }
   }
 }
 
@@ -142,13 +197,22 @@ int cie_rms_norm(void* h, const void* delta, const void* weight, void* out, int6
   auto* hp = static_cast<__half*>(h);
   auto* op = static_cast<__half*>(out);
   const auto* wp = static_cast<const __half*>(weight);
-  if (delta)
-    rms_norm_kernel<true><<<static_cast<unsigned>(ctas), 32 * kWarpsPerCta, 0, s>>>(
-        hp, static_cast<const __half*>(delta), wp, op, rows, hidden, h_stride, delta_stride,
-        out_stride, eps);
-  else
-    rms_norm_kernel<false><<<static_cast<unsigned>(ctas), 32 * kWarpsPerCta, 0, s>>>(
-        hp, nullptr, wp, op, rows, hidden, h_stride, 0, out_stride, eps);
+  const auto* dp = static_cast<const __half*>(delta);
+  const unsigned grid = static_cast<unsigned>(ctas);
+  const int chunks_per_lane = (hidden / 8 + 31) / 32;
+  auto launch = [&](auto kernel) {
+    kernel<<<grid, 32 * kWarpsPerCta, 0, s>>>(hp, dp, wp, op, rows, hidden, h_stride,
+                                              delta ? delta_stride : 0, out_stride, eps);
+  };
+  if (delta) {
+    if (chunks_per_lane <= 4) launch(rms_norm_kernel<true, 4>);
+    else if (chunks_per_lane <= 8) launch(rms_norm_kernel<true, 8>);
+    else launch(rms_norm_kernel<true, 0>);
+  } else {
+    if (chunks_per_lane <= 4) launch(rms_norm_kernel<false, 4>);
+    else if (chunks_per_lane <= 8) launch(rms_norm_kernel<false, 8>);
+    else launch(rms_norm_kernel<false, 0>);
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "rms_norm launch: %s", cudaGetErrorString(e));
   return CIE_OK;
