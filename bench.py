@@ -12,7 +12,9 @@ batch and KV pool: sequences are sharded, no collective on the data path).
 
 Legs:
   value     device time (CUDA events on the launching stream) of K steps
-            with all inputs resident; inputs (537 MB of K/V) exceed L2.
+            with all inputs resident; inputs (537 MB of K/V) exceed L2. The
+            steps run as replays of CUDA graphs of 100 calls each, as the
+            engine's captured decode steps do (--eager: Python launches).
   e2e       the same metric through the C ABI with HOST buffers: every step
             copies q, the K/V pools, lens, slot ids and the block table from
             pinned host memory and reads the output back.
@@ -66,6 +68,9 @@ def parse_args(argv=None):
                     help="skip the Qwen2.5-0.5B-shape model line (serving tok/s)")
     ap.add_argument("--serve-batch", type=int, default=64, help="sequences per GPU")
     ap.add_argument("--serve-steps", type=int, default=128, help="timed decode steps")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch every timed decode call from Python instead of replaying "
+                         "CUDA graphs of them")
     ap.add_argument("--sweep", action="store_true",
                     help="print one JSON line per decode sweep point (configs 2 and 5) "
                          "instead of the benchmark line")
@@ -308,6 +313,7 @@ def workload_config(args, world):
 # ---------------------------------------------------------------------------
 
 L2_FLUSH_BYTES = 256 << 20   # twice the 126 MB L2
+GRAPH_CHUNK = 100            # decode calls per captured graph in the timed loop
 
 
 def time_launches(fn, iters: int, flush: bool, dev):
@@ -495,23 +501,46 @@ def run_ours(args, rank, world, local):
         step()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
-    events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    # The engine calls the decode op inside CUDA graphs (one per decode step),
+    # so by default the timed steps are replays of a graph of `chunk`
+    # consecutive calls (plus one graph for a remainder); --eager launches
+    # every call from Python instead.
+    chunk = min(args.steps, GRAPH_CHUNK)
+    graphs = []
+    if not args.eager:
+        for n in ([chunk] * (args.steps // chunk) + ([args.steps % chunk] if args.steps % chunk else [])):
+            if graphs and n == chunk:
+                graphs.append(graphs[0])
+                continue
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(n):
+                    step()
+            g.replay()
+            graphs.append(g)
+        torch.cuda.synchronize()
+    events = [torch.cuda.Event(enable_timing=True)
+              for _ in range((len(graphs) if graphs else args.steps) + 1)]
     dist_barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(dev.index) as clocks:
         events[0].record(stream)
-        for i in range(args.steps):
-            step()
-            events[i + 1].record(stream)
+        if graphs:
+            for i, g in enumerate(graphs):
+                g.replay()
+                events[i + 1].record(stream)
+        else:
+            for i in range(args.steps):
+                step()
+                events[i + 1].record(stream)
         torch.cuda.synchronize()
     dist_barrier(world)
     torch.cuda.synchronize()
-    per_step_ms = [events[i].elapsed_time(events[i + 1]) for i in range(args.steps)]
     local_ms = events[0].elapsed_time(events[-1])
     total_ms = dist_max(local_ms, world, dev)
     nbytes = decode_bytes(B, L)
     value = nbytes * world * args.steps / (total_ms / 1e3) / 1e9
-    kernel_ms = statistics.mean(per_step_ms)
+    kernel_ms = local_ms / args.steps  # every step is one decode call on this stream
     achieved = nbytes / (kernel_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak_gbs()
     errs = native.device_errors(dev.index, clear=True)
@@ -559,7 +588,10 @@ def run_ours(args, rank, world, local):
             "steps": args.steps, "warmup": max(args.warmup, 3),
             "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16 in / fp32 accumulate", "data": "synthetic",
-            "config": dict(workload_config(args, world), num_splits=S),
+            "config": dict(workload_config(args, world), num_splits=S,
+                           timing=("eager: one Python launch per call" if args.eager else
+                                   f"CUDA graphs of {chunk} consecutive decode calls, replayed "
+                                   f"(the engine's decode steps are CUDA graphs)")),
             "pct_of_peak": 100.0 * achieved / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
