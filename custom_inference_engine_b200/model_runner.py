@@ -16,9 +16,9 @@ By default the decoder body around the attention runs through
 package, about 10 launches per layer); ``fused_body=False`` runs HF's modules.
 
 This is the harness that measures Qwen2.5-0.5B-shape tokens/s and checks greedy
-tokens against HF's own attention. It is not a serving scheduler: there is no
-request queue, admission control or preemption; every slot gets enough pages up
-front for its prompt plus its new tokens.
+tokens against HF's own attention; ``serving.py`` drives it with a request
+queue (Poisson arrivals, continuous batching). Every admitted slot gets enough
+pages up front for its prompt plus its new tokens.
 """
 from __future__ import annotations
 
@@ -159,6 +159,15 @@ class PagedRunner:
         self.kv.lens[slot] = 0
         self.host_lens[slot] = 0
 
+    def release(self, slot: int) -> None:
+        """Return ``slot``'s pages to the pool and clear its history."""
+        n = int((self.kv.block_table[slot] != 0).sum())
+        pages = self.kv.block_table[slot, :n].tolist()
+        self.free_pages.extend(int(p) for p in pages)
+        self.kv.block_table[slot].zero_()
+        self.kv.lens[slot] = 0
+        self.host_lens[slot] = 0
+
     # ---- forward -----------------------------------------------------------
     def _hidden(self, input_ids, position_ids, metadata):
         # the attention lengths of this pass, once for all layers
@@ -195,6 +204,25 @@ class PagedRunner:
         md.write_pages(pages)
         md.write_offsets(offsets)
         return md, positions, cu
+
+    def mixed_step(self, slots, token_chunks) -> list:
+        """One mixed pass: sequence i appends ``token_chunks[i]`` (a decode row is
+        a chunk of one token) to slot ``slots[i]``; returns the greedy token after
+        each chunk's last row."""
+        chunks = [len(c) for c in token_chunks]
+        with torch.inference_mode():
+            md, positions, cu = self.mixed_metadata(slots, chunks)
+            ids = torch.tensor([[t for c in token_chunks for t in c]], dtype=torch.long,
+                               device=self.device)
+            pos = torch.tensor([positions], dtype=torch.long, device=self.device)
+            hidden = self._hidden(ids, pos, md)
+            self.kv.mixed_advance(torch.tensor(slots, dtype=torch.long, device=self.device),
+                                  torch.tensor(chunks, dtype=torch.long, device=self.device))
+            rows = torch.tensor([c - 1 for c in cu[1:]], device=self.device)
+            tokens = self.model.lm_head(hidden[0, rows]).argmax(-1).tolist()
+        for s, c in zip(slots, chunks):
+            self.host_lens[s] += c
+        return tokens
 
     def prefill(self, slots, prompts) -> PrefillResult:
         """Write every prompt into its slot through mixed passes of at most
