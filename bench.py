@@ -490,13 +490,15 @@ def serving_line(args, rank, world, dev):
 
 
 def poisson_line(args, model, rank, world, dev):
-    """Config 4 as specified: each GPU serves its own Poisson stream
-    (``poisson_rate`` requests/s, seed 2000 + rank) of prompts with lognormal
-    lengths (median 512, sigma 0.5, capped at 4096) and outputs of U[64, 512]
-    tokens through the continuous-batching loop (serving.py): 33 slots, a
-    1024-token budget per step, a 32768-token KV pool per GPU. Metrics as the
-    reference's benchmark (5 % trim; host wall clock, since they are request
-    timestamps): tok/s = new tokens of all ranks / longest rank duration."""
+    """Config 4 as specified: one Poisson stream of ``poisson_rate`` x N
+    requests/s (seed 2000) of prompts with lognormal lengths (median 512, sigma
+    0.5, capped at 4096) and outputs of U[64, 512] tokens, sharded round-robin
+    by index over the N GPUs (each GPU sees about ``poisson_rate`` requests/s
+    over the same time window), served per GPU through the continuous-batching
+    loop (serving.py): 33 slots, a 1024-token budget per step, a 32768-token KV
+    pool per GPU. Metrics as the reference's benchmark (5 % trim per GPU; host
+    wall clock, since they are request timestamps): tok/s = new tokens of all
+    GPUs / (latest end - earliest planned arrival over the GPUs)."""
     from custom_inference_engine_b200 import model_runner as MR
     from custom_inference_engine_b200 import serving as SV
 
@@ -504,21 +506,24 @@ def poisson_line(args, model, rank, world, dev):
     runner = MR.PagedRunner(model, max_cache_len=pool_tokens, n_slots=n_slots,
                             token_budget=budget)
     engine = SV.RunnerEngine(runner, n_slots)
-    reqs = SV.poisson_requests(args.poisson_requests, args.poisson_rate, seed=2000 + rank,
-                               vocab=model.config.vocab_size)
+    stream = SV.poisson_requests(args.poisson_requests * world, args.poisson_rate * world,
+                                 seed=2000, vocab=model.config.vocab_size)
+    reqs = stream[rank::world]
     torch.cuda.synchronize()
     dist_barrier(world)
     out, steps = SV.serve(engine, reqs, n_slots=n_slots, token_budget=budget)
     torch.cuda.synchronize()
     m = SV.summarize(out, trim=0.05)
     tokens = dist_sum(float(m["new_tokens"]), world, dev)
-    duration = dist_max(m["duration_s"], world, dev)
+    first = -dist_max(-m["first_planned_s"], world, dev)
+    duration = dist_max(m["last_end_s"], world, dev) - first
     res = {
         "tok_s": tokens / duration, "tok_s_rank0": m["tok_s"], "req_s_rank0": m["req_s"],
         "duration_s": duration, "new_tokens": int(tokens), "n_measured_rank0": m["n_measured"],
         "ttft_ms_rank0": m["ttft_ms"], "tpot_ms_rank0": m["tpot_ms"], "steps_rank0": steps,
         "offered_tok_s": args.poisson_rate * world * 288.0,
-        "workload": f"Poisson {args.poisson_rate:g} req/s per GPU, {args.poisson_requests} "
+        "workload": f"Poisson {args.poisson_rate:g} req/s per GPU ({args.poisson_rate * world:g} "
+                    f"req/s sharded round-robin over {world} GPU(s)), {args.poisson_requests} "
                     f"requests per GPU, prompts lognormal (median 512, sigma 0.5, cap 4096), "
                     f"outputs U[64,512], {n_slots} slots, budget {budget}, KV {pool_tokens} "
                     f"tokens per GPU; 5% trim; host wall clock",

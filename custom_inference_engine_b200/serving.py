@@ -183,6 +183,7 @@ def summarize(requests, trim: float = 0.05) -> dict:
                      if len(r.new_tokens) > 1])
     pct = lambda a, q: float(np.percentile(a, q)) if len(a) else float("nan")
     return {"n_measured": len(m), "duration_s": end - start, "tok_s": tokens / (end - start),
+            "first_planned_s": start, "last_end_s": end,
             "req_s": len(m) / (end - start), "new_tokens": tokens,
             "ttft_ms": {"mean": 1e3 * float(ttft.mean()), "p50": 1e3 * pct(ttft, 50),
                         "p99": 1e3 * pct(ttft, 99)},
