@@ -106,3 +106,51 @@ def test_fused_body_matches_hf_body(cuda_device):
     assert (pre_f.last_logits - pre_h.last_logits).abs().max().item() <= LOGIT_TOL
     assert fused == hf_body
     assert graphed == hf_body
+
+
+def test_logits_follow_the_reference_engine(cuda_device):
+    """Teacher-forced against the REFERENCE ENGINE's own greedy run
+    (tests/golden/make_e2e_golden.py: its attention module and kernels, under
+    the Triton interpreter on CPU, in a 2-layer model initialised on the CPU
+    from seed 0). Fed the reference's tokens, this engine must pick the
+    reference's token at every step whose top-2 logit margin is at least
+    0.02, a token of the reference's top 2 at the three closer calls, and
+    agree on the reference's five largest logits within 0.03 (fp16 logits of
+    magnitude < 4: a few ulps; CPU and GPU GEMMs round differently)."""
+    from conftest import load_golden
+
+    dev = cuda_device
+    g = load_golden("e2e_reference_tokens")
+    lens = g["prompt_lens"].tolist()
+    flat = g["prompts"].tolist()
+    prompts, o = [], 0
+    for n in lens:
+        prompts.append(flat[o:o + n])
+        o += n
+    ref_tok = g["tokens"]          # (B, steps)
+    ref_ids, ref_vals, margins = g["top_ids"], g["top_vals"], g["margins"]
+    cfg = MR.qwen2_config(num_hidden_layers=2, vocab_size=4096, intermediate_size=2048)
+    model = MR.random_qwen2(cfg, seed=int(g["seed"]), device="cpu").to(dev)
+    B = len(prompts)
+    runner = MR.PagedRunner(model, max_cache_len=1024, n_slots=B + 1, token_budget=1024)
+    slots = list(range(1, B + 1))
+    for s in slots:
+        runner.admit(s, 160)
+    pre = runner.prefill(slots, prompts)
+    assert pre.forward_passes == 1
+    steps = [pre.last_logits]
+    graph = runner.decode_graph(slots, ref_tok[:, 0].tolist(), capture=False)
+    for i in range(1, ref_tok.shape[1]):
+        graph.tokens.copy_(ref_tok[:, i - 1].to(dev))
+        graph.step()
+        steps.append(graph.logits.float())
+    for i, logits in enumerate(steps):
+        for b in range(B):
+            ids = ref_ids[b, i].to(dev)
+            got = logits[b, ids].cpu()
+            assert (got - ref_vals[b, i]).abs().max().item() <= 0.03, (b, i)
+            top = int(logits[b].argmax())
+            if margins[b, i] >= 0.02:
+                assert top == int(ref_tok[b, i]), (b, i, top, int(ref_tok[b, i]))
+            else:
+                assert top in ref_ids[b, i, :2].tolist(), (b, i, top)
