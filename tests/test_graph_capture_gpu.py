@@ -102,3 +102,62 @@ def test_mixed_update_and_attention_replay(cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(out[0, rows], eager[0, rows])
     assert native.device_errors(0) == 0
+
+
+def test_one_mixed_graph_serves_changing_batches(cuda_device):
+    """Capturable dynamic-batch mixed attention: ONE graph captured at the
+    largest shape (6 sequences, 96 tokens) replays correctly for batches of
+    1 to 6 sequences with other chunk lengths, cached lengths and slots, all
+    written into the captured device buffers; unused sequences are padded the
+    reference's way (slot 0, cu_seqlens repeating its last value, so L = 0)."""
+    import oracle
+    from custom_inference_engine_b200.attn import core
+
+    dev = cuda_device
+    B_max, T, n_slots, pages_per_slot = 6, 96, 7, 32
+    g = torch.Generator().manual_seed(99)
+    n_pages = 1 + (n_slots - 1) * pages_per_slot
+    k = torch.randn(n_pages, 2, 16, 64, generator=g).half()
+    v = torch.randn(n_pages, 2, 16, 64, generator=g).half()
+    bt = torch.zeros(n_slots, n_pages, dtype=torch.long)
+    perm = torch.randperm(n_pages - 1, generator=g) + 1
+    for s in range(1, n_slots):
+        bt[s, :pages_per_slot] = perm[(s - 1) * pages_per_slot:s * pages_per_slot]
+    kd, vd, btd = k.to(dev), v.to(dev), bt.to(dev)
+    q = torch.zeros(1, T, 14, 64, dtype=torch.half, device=dev)
+    cu = torch.zeros(B_max + 1, dtype=torch.long, device=dev)
+    kvl = torch.zeros(B_max, dtype=torch.long, device=dev)
+    slots = torch.zeros(B_max, dtype=torch.long, device=dev)
+
+    def step():
+        return core.gqa_mixed_attention_op(q, kd, vd, kv_lens=kvl, max_seqlen=T, cu_seqlens=cu,
+                                           slot_ids=slots, block_table=btd)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = step()
+    compositions = [([1], [300], [4]),
+                    ([40, 1, 1, 30], [0, 77, 250, 12], [2, 5, 1, 6]),
+                    ([16, 16, 16, 16, 16, 16], [3, 100, 0, 401, 64, 17], [6, 5, 4, 3, 2, 1]),
+                    ([1, 95], [20, 200], [3, 1])]
+    for chunks, kv_lens, sl in compositions:
+        n = len(chunks)
+        cum = [0]
+        for c in chunks:
+            cum.append(cum[-1] + c)
+        cu.copy_(torch.tensor(cum + [cum[-1]] * (B_max - n)))
+        kvl.copy_(torch.tensor(kv_lens + [0] * (B_max - n)))
+        slots.copy_(torch.tensor(sl + [0] * (B_max - n)))
+        q.copy_(torch.randn(1, T, 14, 64, generator=g).half())
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = oracle.mixed_attention_fp32(q.cpu(), k, v, T, cu.cpu(), kvl.cpu(), slots.cpu(), bt)
+        rows = slice(0, cum[-1])
+        err = (out[0, rows].float().cpu() - ref[0, rows].float()).abs().max().item()
+        assert err <= 2e-3, (chunks, err)
+    assert native.device_errors(0) == 0
