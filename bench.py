@@ -462,7 +462,8 @@ def serving_line(args, rank, world, dev):
     Random-init model (HF initialiser, N(0, 0.02), seed 0, fp16). Per GPU,
     ``serve_batch`` prompts of uniform random ids with lognormal lengths (median
     512, sigma 0.5, capped at 4096; seed 1000 + rank) are prefilled through the
-    mixed op in passes of at most 2048 tokens, then ``serve_steps`` greedy decode
+    mixed op in passes of at most 2048 tokens (each a replay of the CUDA graph
+    of its token bucket, captured before timing), then ``serve_steps`` greedy decode
     steps run as one CUDA graph each (embedding, 24 layers with the paged decode
     op and the KV scatter, lm_head, argmax). Decode tok/s = sequences x steps of
     all ranks / max-over-ranks device time; the last step's tokens are read back
@@ -483,6 +484,7 @@ def serving_line(args, rank, world, dev):
     slots = list(range(1, B + 1))
     for s, c in zip(slots, cap):
         runner.admit(s, c)
+    runner.capture_mixed_graphs()
     stream = torch.cuda.current_stream()
     dist_barrier(world)
     torch.cuda.synchronize()

@@ -25,6 +25,7 @@ from __future__ import annotations
 import math
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 # Qwen2.5-0.5B-Instruct architecture (the reference's model, README.md:3).
@@ -127,7 +128,7 @@ class PagedRunner:
     """
 
     def __init__(self, model, max_cache_len: int, n_slots: int, page_seed: int = 0,
-                 token_budget: int = 2048, fused_body: bool = True):
+                 token_budget: int = 2048, fused_body: bool = True, mixed_graphs: bool = True):
         from .attn.core import use_cuda_attention
         from .kv_cache.storage import KVStorage
 
@@ -141,9 +142,17 @@ class PagedRunner:
         self.free_pages = (torch.randperm(self.kv.n_pages - 1, generator=g) + 1).tolist()
         self.token_budget = token_budget
         self.host_lens = [0] * n_slots  # host mirror of kv.lens
+        self.host_pages = {}            # slot -> its pages (host mirror of the block-table row)
         # fused_body: the CUDA element-wise kernels around the attention
         # (FusedQwen2Body); False runs HF's Qwen2Model modules as they are
         self.body = FusedQwen2Body(model, max_cache_len) if fused_body else None
+        # mixed_graphs: mixed passes replay a CUDA graph per token bucket (the
+        # reference's FullMixedModule); False runs them eagerly
+        self.use_mixed_graphs = mixed_graphs and self.device.type == "cuda"
+        self.mixed_buckets = sorted({b for b in MIXED_TOKEN_BUCKETS if b < token_budget}
+                                    | {token_budget})
+        self._mixed_graphs = {}
+        self._graph_pool = None
 
     # ---- slots -------------------------------------------------------------
     def admit(self, slot: int, capacity_tokens: int) -> None:
@@ -154,16 +163,15 @@ class PagedRunner:
         if n > len(self.free_pages):
             raise RuntimeError(f"page pool exhausted: need {n}, {len(self.free_pages)} free")
         pages, self.free_pages = self.free_pages[:n], self.free_pages[n:]
+        self.host_pages[slot] = np.asarray(pages, dtype=np.int64)
         self.kv.block_table[slot].zero_()
-        self.kv.block_table[slot, :n] = torch.tensor(pages, dtype=torch.long)
+        self.kv.block_table[slot, :n] = torch.from_numpy(self.host_pages[slot])
         self.kv.lens[slot] = 0
         self.host_lens[slot] = 0
 
     def release(self, slot: int) -> None:
         """Return ``slot``'s pages to the pool and clear its history."""
-        n = int((self.kv.block_table[slot] != 0).sum())
-        pages = self.kv.block_table[slot, :n].tolist()
-        self.free_pages.extend(int(p) for p in pages)
+        self.free_pages.extend(int(p) for p in self.host_pages.pop(slot, ()))
         self.kv.block_table[slot].zero_()
         self.kv.lens[slot] = 0
         self.host_lens[slot] = 0
@@ -180,49 +188,79 @@ class PagedRunner:
                                metadata=metadata, use_cache=False)
         return out.last_hidden_state
 
-    def mixed_metadata(self, slots, chunks):
-        """AttentionMetadata of one mixed pass: sequence i appends ``chunks[i]``
+    def placement(self, slots, chunks):
+        """Positions, pages and in-page offsets (numpy, one per token) and
+        cu_seqlens of a mixed pass in which sequence i appends ``chunks[i]``
         tokens to slot ``slots[i]`` at positions host_lens[slot] onward."""
+        T = int(sum(chunks))
+        ch = np.asarray(chunks, dtype=np.int64)
+        cu = np.concatenate([[0], np.cumsum(ch)])
+        seq = np.repeat(np.arange(len(slots)), ch)          # sequence of every token
+        starts = np.asarray([self.host_lens[s] for s in slots], dtype=np.int64)
+        positions = starts[seq] + np.arange(T, dtype=np.int64) - cu[seq]
+        pages = np.empty(T, dtype=np.int64)
+        for i, s in enumerate(slots):
+            pages[cu[i]:cu[i + 1]] = self.host_pages[s][positions[cu[i]:cu[i + 1]] // PAGE_SIZE]
+        offsets = positions % PAGE_SIZE
+        return positions, pages, offsets, cu
+
+    def mixed_metadata(self, slots, chunks):
+        """AttentionMetadata of one mixed pass (see ``placement``)."""
         from .attn.metadata import AttentionMetadata
 
-        T = sum(chunks)
-        md = AttentionMetadata(token_count=T, full_decode=False, device=self.device)
+        positions, pages, offsets, cu = self.placement(slots, chunks)
+        md = AttentionMetadata(token_count=int(cu[-1]), full_decode=False, device=self.device)
         md.prepare_full_graph(len(slots))
         md.write_slot_ids(slots)
-        cu = [0]
-        pages, offsets, positions = [], [], []
-        bt = self.kv.block_table
-        rows = bt[torch.tensor(slots)].cpu()
-        for i, (s, c) in enumerate(zip(slots, chunks)):
-            start = self.host_lens[s]
-            pos = list(range(start, start + c))
-            positions += pos
-            pages += [int(rows[i, p // PAGE_SIZE]) for p in pos]
-            offsets += [p % PAGE_SIZE for p in pos]
-            cu.append(cu[-1] + c)
         md.write_cu_seqlens(cu)
         md.write_pages(pages)
         md.write_offsets(offsets)
-        return md, positions, cu
+        return md, positions, cu.tolist()
+
+    def mixed_graph(self, tokens: int) -> "MixedGraph":
+        """The captured mixed pass of the smallest token bucket >= ``tokens``."""
+        b = next(x for x in self.mixed_buckets if x >= tokens)
+        if b not in self._mixed_graphs:
+            if self._graph_pool is None:
+                self._graph_pool = torch.cuda.graph_pool_handle()
+            self._mixed_graphs[b] = MixedGraph(self, b, self.kv.n_slots - 1, self._graph_pool)
+        return self._mixed_graphs[b]
+
+    def capture_mixed_graphs(self) -> None:
+        """Capture every token bucket's mixed pass now (capture takes tens of
+        milliseconds; do it before anything is timed)."""
+        if self.use_mixed_graphs:
+            for b in self.mixed_buckets:
+                self.mixed_graph(b)
+
+    def mixed_logits(self, slots, token_chunks):
+        """One mixed pass (sequence i appends ``token_chunks[i]`` to slot
+        ``slots[i]``); returns the logits at each chunk's last row (n, vocab),
+        from a captured graph when ``mixed_graphs`` is on."""
+        chunks = [len(c) for c in token_chunks]
+        flat = [t for c in token_chunks for t in c]
+        with torch.inference_mode():
+            if self.use_mixed_graphs and len(slots) <= self.kv.n_slots - 1 and \
+                    sum(chunks) <= self.mixed_buckets[-1]:
+                logits = self.mixed_graph(sum(chunks)).run(slots, chunks, flat)
+            else:
+                md, positions, cu = self.mixed_metadata(slots, chunks)
+                ids = torch.tensor([flat], dtype=torch.long, device=self.device)
+                pos = torch.from_numpy(positions).view(1, -1).to(self.device)
+                hidden = self._hidden(ids, pos, md)
+                self.kv.mixed_advance(torch.tensor(slots, dtype=torch.long, device=self.device),
+                                      torch.tensor(chunks, dtype=torch.long, device=self.device))
+                rows = torch.tensor([c - 1 for c in cu[1:]], device=self.device)
+                logits = self.model.lm_head(hidden[0, rows])
+        for s, c in zip(slots, chunks):
+            self.host_lens[s] += c
+        return logits
 
     def mixed_step(self, slots, token_chunks) -> list:
         """One mixed pass: sequence i appends ``token_chunks[i]`` (a decode row is
         a chunk of one token) to slot ``slots[i]``; returns the greedy token after
         each chunk's last row."""
-        chunks = [len(c) for c in token_chunks]
-        with torch.inference_mode():
-            md, positions, cu = self.mixed_metadata(slots, chunks)
-            ids = torch.tensor([[t for c in token_chunks for t in c]], dtype=torch.long,
-                               device=self.device)
-            pos = torch.tensor([positions], dtype=torch.long, device=self.device)
-            hidden = self._hidden(ids, pos, md)
-            self.kv.mixed_advance(torch.tensor(slots, dtype=torch.long, device=self.device),
-                                  torch.tensor(chunks, dtype=torch.long, device=self.device))
-            rows = torch.tensor([c - 1 for c in cu[1:]], device=self.device)
-            tokens = self.model.lm_head(hidden[0, rows]).argmax(-1).tolist()
-        for s, c in zip(slots, chunks):
-            self.host_lens[s] += c
-        return tokens
+        return self.mixed_logits(slots, token_chunks).argmax(-1).tolist()
 
     def prefill(self, slots, prompts) -> PrefillResult:
         """Write every prompt into its slot through mixed passes of at most
@@ -234,33 +272,19 @@ class PagedRunner:
         with torch.inference_mode():
             while any(remaining):
                 budget = self.token_budget
-                sel, chunks, toks = [], [], []
+                sel, chunks = [], []
                 for i, r in enumerate(remaining):
                     if r and budget > 0:
                         c = min(len(r), budget)
                         sel.append(i)
                         chunks.append(c)
-                        toks += r[:c]
                         budget -= c
                 batch_slots = [slots[i] for i in sel]
-                md, positions, cu = self.mixed_metadata(batch_slots, chunks)
-                ids = torch.tensor([toks], dtype=torch.long, device=self.device)
-                pos = torch.tensor([positions], dtype=torch.long, device=self.device)
-                hidden = self._hidden(ids, pos, md)
-                slot_t = torch.tensor(batch_slots, dtype=torch.long, device=self.device)
-                len_t = torch.tensor(chunks, dtype=torch.long, device=self.device)
-                self.kv.mixed_advance(slot_t, len_t)
-                last_rows = []
+                logits = self.mixed_logits(batch_slots, [remaining[i][:c] for i, c in zip(sel, chunks)])
                 for j, i in enumerate(sel):
-                    self.host_lens[slots[i]] += chunks[j]
                     remaining[i] = remaining[i][chunks[j]:]
                     if not remaining[i]:
-                        last_rows.append((i, cu[j + 1] - 1))
-                if last_rows:
-                    rows = torch.tensor([r for _, r in last_rows], device=self.device)
-                    logits = self.model.lm_head(hidden[0, rows]).float()
-                    for (i, _), lg in zip(last_rows, logits):
-                        done_logits[i] = lg
+                        done_logits[i] = logits[j].float()
                 passes += 1
         last = torch.stack(done_logits)
         return PrefillResult(first_tokens=last.argmax(-1).tolist(), last_logits=last,
@@ -323,3 +347,71 @@ class DecodeGraph:
         for s in self.slots:
             self.runner.host_lens[s] += 1
         return self.tokens
+
+
+MIXED_TOKEN_BUCKETS = (64, 128, 256, 512, 1024, 2048)
+
+
+class MixedGraph:
+    """One mixed pass of up to ``max_seqs`` sequences and ``tokens`` tokens,
+    captured in a CUDA graph (the reference's FullMixedModule): the metadata,
+    token ids, positions, last-row indices and the length advance live in
+    static buffers written before each replay. Tokens past the pass's own are
+    padding the reference's way: page 0, offset 0, position 0, outside every
+    sequence (cu_seqlens repeats its last value); absent sequences are slot 0
+    with no tokens. ``run`` returns the logits at each sequence's last row."""
+
+    def __init__(self, runner, tokens: int, max_seqs: int, pool=None):
+        from .attn.metadata import AttentionMetadata
+
+        self.runner = runner
+        self.tokens = tokens
+        self.max_seqs = max_seqs
+        dev = runner.device
+        self.md = AttentionMetadata(token_count=tokens, full_decode=False, device=dev)
+        self.md.prepare_full_graph(max_seqs)
+        z = lambda n: torch.zeros(n, dtype=torch.long, device=dev)
+        self.ids, self.pos = z((1, tokens)), z((1, tokens))
+        self.last_rows, self.adv_slots, self.adv_lens = z(max_seqs), z(max_seqs), z(max_seqs)
+        self.logits = None
+        saved = runner.kv.lens.clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side), torch.inference_mode():
+            self._pass()
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.inference_mode(), torch.cuda.graph(self.graph, pool=pool):
+            self._pass()
+        runner.kv.lens.copy_(saved)
+
+    def _pass(self):
+        r = self.runner
+        hidden = r._hidden(self.ids, self.pos, self.md)
+        self.logits = r.model.lm_head(hidden[0, self.last_rows])
+        r.kv.mixed_advance(self.adv_slots, self.adv_lens)
+
+    def run(self, slots, chunks, flat_tokens):
+        n, T = len(slots), int(sum(chunks))
+        positions, pages, offsets, cu = self.runner.placement(slots, chunks)
+        md = self.md
+        md.write_slot_ids(slots)
+        md.write_cu_seqlens(cu)
+        md.write_pages(pages)
+        md.write_offsets(offsets)
+        ids = np.zeros(self.tokens, dtype=np.int64)
+        ids[:T] = flat_tokens
+        pos = np.zeros(self.tokens, dtype=np.int64)
+        pos[:T] = positions
+        small = np.zeros((3, self.max_seqs), dtype=np.int64)
+        small[0, :n] = cu[1:] - 1
+        small[1, :n] = slots
+        small[2, :n] = chunks
+        self.ids.copy_(torch.from_numpy(ids).view(1, -1))
+        self.pos.copy_(torch.from_numpy(pos).view(1, -1))
+        small_d = torch.from_numpy(small).to(self.ids.device)
+        self.last_rows.copy_(small_d[0])
+        self.adv_slots.copy_(small_d[1])
+        self.adv_lens.copy_(small_d[2])
+        self.graph.replay()
+        return self.logits[:n]

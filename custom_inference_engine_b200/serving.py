@@ -12,7 +12,8 @@ benchmark/metrics.py:54-75, 159-200):
   time has passed are admitted into free slots with what budget is left
   (scheduler.py:372-433);
 * a step with prefill work is ONE mixed pass through
-  ``inference::gqa_mixed_attention`` (decode rows are chunks of one token); a
+  ``inference::gqa_mixed_attention`` (decode rows are chunks of one token),
+  replayed from the CUDA graph of the smallest token bucket that holds it; a
   step with only decode rows replays the CUDA graph of the smallest batch
   bucket that holds them (rows beyond the batch use the padding slot 0);
 * a request finishes after ``max_new`` tokens (the end-of-sequence id of the
@@ -192,12 +193,13 @@ def summarize(requests, trim: float = 0.05) -> dict:
 
 
 class RunnerEngine:
-    """``serve``'s engine on a ``PagedRunner``: mixed passes eagerly, decode
-    steps from the captured buckets."""
+    """``serve``'s engine on a ``PagedRunner``: mixed passes and decode steps
+    from CUDA graphs captured per token bucket and per batch bucket."""
 
     def __init__(self, runner, n_slots: int):
         self.runner = runner
         self.buckets = DecodeBuckets(runner, n_slots - 1)
+        runner.capture_mixed_graphs()
 
     @property
     def free_pages(self):

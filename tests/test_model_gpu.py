@@ -154,3 +154,22 @@ def test_logits_follow_the_reference_engine(cuda_device):
                 assert top == int(ref_tok[b, i]), (b, i, top, int(ref_tok[b, i]))
             else:
                 assert top in ref_ids[b, i, :2].tolist(), (b, i, top)
+
+
+def test_mixed_graphs_match_eager_passes(cuda_device):
+    """Prefill through captured mixed passes (token buckets, padded metadata)
+    gives the tokens and, within fp16 noise, the logits of eager passes."""
+    model = _model(cuda_device)
+    prompts = _prompts()
+    out = {}
+    for graphs in (False, True):
+        runner = MR.PagedRunner(model, max_cache_len=4096, n_slots=8, token_budget=64,
+                                mixed_graphs=graphs)
+        slots = list(range(1, len(prompts) + 1))
+        for s, p in zip(slots, prompts):
+            runner.admit(s, len(p) + 4)
+        out[graphs] = runner.prefill(slots, prompts)
+        assert runner.host_lens[1:len(prompts) + 1] == [len(p) for p in prompts]
+        assert runner.kv.lens[1:len(prompts) + 1].tolist() == [len(p) for p in prompts]
+    assert out[True].first_tokens == out[False].first_tokens
+    assert (out[True].last_logits - out[False].last_logits).abs().max().item() <= LOGIT_TOL

@@ -28,10 +28,21 @@ def test_mixed_metadata_places_every_token():
     r.host_lens[3] = 20  # slot 3 already holds 20 tokens
     md, positions, cu = r.mixed_metadata([1, 3], [5, 14])
     assert cu == [0, 5, 19]
-    assert positions == list(range(5)) + list(range(20, 34))
+    assert positions.tolist() == list(range(5)) + list(range(20, 34))
     bt = r.kv.block_table
     for t, (s, pos) in enumerate([(1, p) for p in range(5)] + [(3, p) for p in range(20, 34)]):
         assert int(md.pages[t]) == int(bt[s, pos // 16])
         assert int(md.offsets[t]) == pos % 16
     assert md.slot_ids.tolist() == [1, 3] and md.cu_seqlens.tolist() == [0, 5, 19]
     assert not md.full_decode and md.max_seqlen == 19
+
+
+def test_release_returns_pages_and_clears_the_slot():
+    r = _runner()
+    free = len(r.free_pages)
+    r.admit(2, 50)
+    assert len(r.free_pages) == free - 4
+    r.host_lens[2] = 9
+    r.release(2)
+    assert len(r.free_pages) == free and r.host_lens[2] == 0
+    assert r.kv.block_table[2].eq(0).all() and int(r.kv.lens[2]) == 0
