@@ -31,6 +31,7 @@ gqa_decode_attention_op = torch.ops.inference.gqa_decode_attention
 gqa_mixed_attention_op = torch.ops.inference.gqa_mixed_attention
 rope_kv_decode_update_op = torch.ops.inference.rope_kv_decode_update
 rope_kv_mixed_update_op = torch.ops.inference.rope_kv_mixed_update
+rope_kv_decode_attention_op = torch.ops.inference.rope_kv_decode_attention
 _gqa_decode_attention_splits = torch.ops.inference.gqa_decode_attention_splits
 
 # The reference tunes Triton tiles here (attn/core.py:114-116). The CUDA decode
@@ -89,16 +90,25 @@ class TritonQwen2Attention(torch.nn.Module):
     """HF ``Qwen2Attention`` replacement that runs the paged CUDA attention.
 
     With ``kv_manager`` (a ``KVStorage``) and ``metadata`` (an
-    ``AttentionMetadata``) it computes the fused QKV projection, then ONE launch
-    rotates q and k and writes the new K/V rows into the pages (the decode or
-    the mixed addressing of ``KVStorage.decode_update`` / ``mixed_update``,
-    bit-identical to HF's ``apply_rotary_pos_emb`` followed by those updates),
-    runs the matching attention op, then ``o_proj``. ``fuse_rope = False``
-    restores the reference's sequence (HF RoPE, then ``kv_manager``'s update
-    methods). Without ``kv_manager`` it defers to the wrapped HF module.
+    ``AttentionMetadata``) it computes the fused QKV projection, then:
+
+    * decode pass: ONE launch (``inference::rope_kv_decode_attention``) rotates
+      q and k, writes the new K/V row of every token into its page and runs the
+      decode attention over the slot's keys, the new one included;
+    * mixed pass: one launch rotates q and k and writes the new K/V rows
+      (``inference::rope_kv_mixed_update``), then the mixed attention op;
+
+    then ``o_proj``. The results are bit-identical to HF's
+    ``apply_rotary_pos_emb`` followed by ``KVStorage.decode_update`` /
+    ``mixed_update`` and the attention op. ``fuse_decode_attention = False``
+    splits the decode pass into the RoPE + KV launch and the attention op;
+    ``fuse_rope = False`` restores the reference's sequence (HF RoPE, then
+    ``kv_manager``'s update methods). Without ``kv_manager`` it defers to the
+    wrapped HF module.
     """
 
     fuse_rope = True
+    fuse_decode_attention = True
 
     def __init__(self, original_attn):
         super().__init__()
@@ -135,6 +145,12 @@ class TritonQwen2Attention(torch.nn.Module):
         qkv = torch.nn.functional.linear(hidden_states, self.qkv_weight, self.qkv_bias)
         cos, sin = position_embeddings
         layer = self.layer_idx
+        if self.fuse_rope and self.fuse_decode_attention and metadata.full_decode:
+            # RoPE, K/V write and decode attention: one launch
+            o = rope_kv_decode_attention_op(qkv, cos, sin, kv_manager.keys[layer],
+                                            kv_manager.values[layer], kv_manager.lens,
+                                            metadata.slot_ids, kv_manager.block_table)
+            return self.original.o_proj(o.reshape(1, total_T, self.num_heads * self.head_dim)), None
         if self.fuse_rope:
             if metadata.full_decode:
                 q = rope_kv_decode_update_op(qkv, cos, sin, kv_manager.keys[layer],

@@ -145,3 +145,26 @@ def rope_kv_mixed_update(qkv, cos, sin, k_cache, v_cache, pages, offsets, out=No
         k_cache.stride(1), native.stream_ptr(stream))
     native.check(st, "cie_rope_kv_mixed_update")
     return out
+
+
+def rope_kv_decode_attention(qkv, cos, sin, k_cache, v_cache, lens, slot_ids, block_table,
+                             out=None, num_splits: int = 0, workspace=None, stream=None):
+    """cie_rope_kv_decode_attention: rotary embedding, K/V write of each token
+    at its slot's current length (``lens`` per slot, not advanced) and decode
+    attention over the slot's keys including the new one, in one launch."""
+    out, hq = _rope_q_out(qkv, k_cache, out)
+    B = slot_ids.shape[0]
+    d = k_cache.shape[3]
+    S = num_splits if num_splits > 0 else decode_default_splits(B, qkv.device.index or 0)
+    need = decode_workspace_bytes(B, hq, d, S)
+    if need > 0 and workspace is None:
+        workspace = torch.empty(need // 4, dtype=torch.float32, device=qkv.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    st = native.lib().cie_rope_kv_decode_attention(
+        _p(qkv), qkv.stride(1), _p(cos), _p(sin), cos.stride(1), _p(k_cache), _p(v_cache),
+        _p(lens), _p(slot_ids), _p(block_table), _p(out), _p(workspace), ws_bytes, B, hq,
+        k_cache.shape[1], d, k_cache.shape[2], k_cache.shape[0],
+        min(lens.shape[0], block_table.shape[0]), block_table.stride(0), k_cache.stride(0),
+        k_cache.stride(1), S, native.stream_ptr(stream))
+    native.check(st, "cie_rope_kv_decode_attention")
+    return out

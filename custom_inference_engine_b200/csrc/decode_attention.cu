@@ -61,7 +61,48 @@ struct Params {
   int64_t n_pages;
   int64_t n_slots;
   int64_t bt_stride;
+  // Fused rotary embedding + KV write (cie_rope_kv_decode_attention), when qkv
+  // is set: q comes from the fused QKV projection and is rotated in
+  // registers; lens is then per SLOT (the length before this token), the
+  // token sits at position lens[slot] and attends to lens[slot] + 1 keys; its
+  // rotated k and its v are written to the pool and into the shared-memory
+  // copy of their page.
+  const __half* qkv;          // (B, (H_q + 2 H_kv) * D), row stride qkv_tok
+  int64_t qkv_tok;
+  const __half* cos;          // (B, D), row stride cs_tok
+  const __half* sin;
+  int64_t cs_tok;
+  __half* k_cache;            // the pools, for the new row
+  __half* v_cache;
+  int64_t page_stride, head_stride;
 };
+
+// x * c + rot * s on 8 fp16 values, each operation rounded to fp16 (no fused
+// multiply-add): transformers' apply_rotary_pos_emb step by step.
+__device__ __forceinline__ uint4 rope8(uint4 x, uint4 rot, uint4 c, uint4 sn) {
+  uint4 r;
+  const __half2* xh = reinterpret_cast<const __half2*>(&x);
+  const __half2* rh = reinterpret_cast<const __half2*>(&rot);
+  const __half2* ch = reinterpret_cast<const __half2*>(&c);
+  const __half2* sh = reinterpret_cast<const __half2*>(&sn);
+  __half2* oh = reinterpret_cast<__half2*>(&r);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) oh[e] = __hadd2_rn(__hmul2_rn(xh[e], ch[e]), __hmul2_rn(rh[e], sh[e]));
+  return r;
+}
+
+__device__ __forceinline__ uint4 neg8(uint4 x) {
+  const __half2* xh = reinterpret_cast<const __half2*>(&x);
+  uint4 r;
+  __half2* oh = reinterpret_cast<__half2*>(&r);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) oh[e] = __hneg2(xh[e]);
+  return r;
+}
+
+__device__ __forceinline__ uint4 ldg16(const __half* ptr) {
+  return __ldg(reinterpret_cast<const uint4*>(ptr));
+}
 
 // Fewest pages a split is given: below this the fixed cost of a CTA (start-up,
 // first TMA round trip, its partial) outweighs the bytes it streams.
@@ -70,10 +111,12 @@ constexpr int kMinPagesPerSplit = 4;
 // Pages of sequence b that the kernels visit; 0 for an invalid slot. A length
 // beyond the block-table row is clamped to it.
 __device__ __forceinline__ int seq_pages(const int64_t* lens, const int64_t* slot_ids, int b,
-                                         int64_t n_slots, int64_t bt_stride) {
+                                         int64_t n_slots, int64_t bt_stride, int lens_per_slot) {
   const int64_t slot = slot_ids[b];
   if (slot < 0 || slot >= n_slots) return 0;
-  int64_t L = lens[b];
+  // per sequence: keys visible to the query; per slot: the slot's length
+  // before the query token, which is then written and attended to as well
+  int64_t L = lens_per_slot ? lens[slot] + 1 : lens[b];
   if (L < 0) L = 0;
   const int64_t np = (L + kPage - 1) / kPage;
   return static_cast<int>(np > bt_stride ? bt_stride : np);
@@ -121,16 +164,18 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
 
   // ---- per-sequence page range of this split -------------------------------
   int64_t slot = p.slot_ids[b];
-  int64_t L = p.lens[b];
   bool bad = false;
   if (slot < 0 || slot >= p.n_slots) {
     if (threadIdx.x == 0) raise_error(CIE_DEVERR_BAD_SLOT);
     bad = true;
   }
+  int64_t L = p.qkv == nullptr ? p.lens[b] : (bad ? 0 : p.lens[slot] + 1);
   if (L < 0) L = 0;
+  bool clamped = false;
   if (!bad && (L + kPage - 1) / kPage > p.bt_stride) {
     if (threadIdx.x == 0) raise_error(CIE_DEVERR_BAD_LENGTH);
     L = p.bt_stride * kPage;
+    clamped = true;
   }
   if (bad) L = 0;
   const int n_seq_pages = static_cast<int>((L + kPage - 1) / kPage);
@@ -216,7 +261,7 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
 
   // Q^T as the B operand: b0 = Q[g][16ks + 2t4 .. +1], b1 = Q[g][16ks + 8 + 2t4 .. +1]
   uint32_t bq[4][2];
-  {
+  if (p.qkv == nullptr) {
     const bool valid = g < kGroup;
     const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
         p.q + (static_cast<int64_t>(b) * H_Q + h * kGroup + (valid ? g : 0)) * kD);
@@ -225,7 +270,28 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
       bq[ks][0] = valid ? qrow[(ks * 16 + 2 * t4) >> 1] : 0u;
       bq[ks][1] = valid ? qrow[(ks * 16 + 8 + 2 * t4) >> 1] : 0u;
     }
+  } else {
+    // rotate_half(x)[e] = -x[e + 32] (e < 32), x[e - 32] (e >= 32)
+    const bool valid = g < kGroup && !bad;
+    const __half2* qrow = reinterpret_cast<const __half2*>(
+        p.qkv + static_cast<int64_t>(b) * p.qkv_tok + (h * kGroup + (valid ? g : 0)) * kD);
+    const __half2* cs = reinterpret_cast<const __half2*>(p.cos + static_cast<int64_t>(b) * p.cs_tok);
+    const __half2* sn = reinterpret_cast<const __half2*>(p.sin + static_cast<int64_t>(b) * p.cs_tok);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int e = ks * 16 + hf * 8 + 2 * t4;  // even: (e, e + 1) in one half
+        const __half2 x = qrow[e >> 1];
+        const __half2 rot = e < 32 ? __hneg2(qrow[(e + 32) >> 1]) : qrow[(e - 32) >> 1];
+        const __half2 r = __hadd2_rn(__hmul2_rn(x, cs[e >> 1]), __hmul2_rn(rot, sn[e >> 1]));
+        bq[ks][hf] = valid ? *reinterpret_cast<const uint32_t*>(&r) : 0u;
+      }
+    }
   }
+  // fused mode: the page (index in this split) holding the new token, and its row
+  const int new_i = (p.qkv != nullptr && Li > 0 && !clamped) ? (Li - 1) / kPage - page_begin : -1;
+  const int new_row = (Li - 1) & (kPage - 1);
 
   constexpr float kScale = 0.125f;  // head_dim ** -0.5 for D = 64
   float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F;  // heads 2*t4, 2*t4+1
@@ -246,6 +312,35 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
     // 128B-swizzle phase of row r is r mod 8.
     const uint32_t kt = ring_u32 + s * C::kStageBytes + h * kHeadTileBytes;
     const uint32_t vt = kt + HKV * kHeadTileBytes;
+    if (i == new_i) {
+      // the new token: rotated k and v of kv head h into this page's row, in
+      // shared memory (for this attention) and in the pool (for later steps);
+      // lanes 0-7 own k chunks, lanes 8-15 v chunks of 8 elements
+      if (lane < 16) {
+        const int c = lane & 7;
+        const __half* src = p.qkv + static_cast<int64_t>(b) * p.qkv_tok +
+                            ((lane < 8 ? H_Q : H_Q + HKV) + h) * kD;
+        uint4 val = ldg16(src + c * 8);
+        if (lane < 8) {
+          const __half* cs = p.cos + static_cast<int64_t>(b) * p.cs_tok + c * 8;
+          const __half* sn = p.sin + static_cast<int64_t>(b) * p.cs_tok + c * 8;
+          const uint4 partner = ldg16(src + (c ^ 4) * 8);
+          val = rope8(val, c < 4 ? neg8(partner) : partner, ldg16(cs), ldg16(sn));
+        }
+        const uint32_t saddr = (lane < 8 ? kt : vt) + sw128(new_row, c);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(val.x),
+                     "r"(val.y), "r"(val.z), "r"(val.w)
+                     : "memory");
+        int64_t pg = p.block_table[slot * p.bt_stride + (Li - 1) / kPage];
+        if (pg >= 0 && pg < p.n_pages) {
+          __half* dst = (lane < 8 ? p.k_cache : p.v_cache) + pg * p.page_stride +
+                        h * p.head_stride + new_row * kD + c * 8;
+          *reinterpret_cast<uint4*>(dst) = val;
+        }
+      }
+      fence_proxy_async_smem();  // the stage is refilled by TMA later
+      __syncwarp();
+    }
 
     // S^T (16 keys x 8 heads) = K (16 x 64) . Q^T (64 x 8)
     float sc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -414,7 +509,7 @@ __global__ void __launch_bounds__(256)
     decode_merge_kernel(const float* __restrict__ ws_acc, const float* __restrict__ ws_ml,
                         __half* __restrict__ o, const int64_t* __restrict__ lens,
                         const int64_t* __restrict__ slot_ids, int64_t n_slots,
-                        int64_t bt_stride, int num_splits, int num_q_heads) {
+                        int64_t bt_stride, int num_splits, int num_q_heads, int lens_per_slot) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float s_m[8], s_l[8];
   __shared__ float2 s_acc[8][32];
@@ -423,7 +518,7 @@ __global__ void __launch_bounds__(256)
   const int S = num_splits;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int np = seq_pages(lens, slot_ids, b, n_slots, bt_stride);
+  const int np = seq_pages(lens, slot_ids, b, n_slots, bt_stride, lens_per_slot);
   const int pps = split_pages(np, S);
   const int active = np == 0 ? 0 : (np + pps - 1) / pps;
 
@@ -468,11 +563,20 @@ __global__ void __launch_bounds__(256)
       __floats2half2_rn(num.x * inv, num.y * inv);
 }
 
+// Arguments of the fused rotary embedding + KV write (see Params).
+struct FusedRope {
+  const void* qkv;
+  int64_t qkv_tok;
+  const void* cos;
+  const void* sin;
+  int64_t cs_tok;
+};
+
 template <int HKV>
 int launch(const void* q, const void* k, const void* v, const int64_t* lens,
            const int64_t* slot_ids, const int64_t* block_table, void* o, float* ws, int batch,
            int64_t n_pages, int64_t n_slots, int64_t bt_stride, int64_t page_stride,
-           int64_t head_stride, int S, cudaStream_t stream) {
+           int64_t head_stride, int S, cudaStream_t stream, const FusedRope* rope = nullptr) {
   using C = Cfg<HKV>;
   CUtensorMap tm_k, tm_v;
   const uint64_t dims[4] = {kD, kPage, HKV, static_cast<uint64_t>(n_pages)};
@@ -503,6 +607,22 @@ int launch(const void* q, const void* k, const void* v, const int64_t* lens,
   p.n_pages = n_pages;
   p.n_slots = n_slots;
   p.bt_stride = bt_stride;
+  p.qkv = nullptr;
+  p.qkv_tok = 0;
+  p.cos = p.sin = nullptr;
+  p.cs_tok = 0;
+  p.k_cache = p.v_cache = nullptr;
+  p.page_stride = page_stride;
+  p.head_stride = head_stride;
+  if (rope != nullptr) {
+    p.qkv = static_cast<const __half*>(rope->qkv);
+    p.qkv_tok = rope->qkv_tok;
+    p.cos = static_cast<const __half*>(rope->cos);
+    p.sin = static_cast<const __half*>(rope->sin);
+    p.cs_tok = rope->cs_tok;
+    p.k_cache = static_cast<__half*>(const_cast<void*>(k));
+    p.v_cache = static_cast<__half*>(const_cast<void*>(v));
+  }
   dim3 grid(S, batch);
   decode_split_kernel<HKV><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tm_k, tm_v, p);
   cudaError_t e = cudaGetLastError();
@@ -520,7 +640,7 @@ int launch(const void* q, const void* k, const void* v, const int64_t* lens,
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, decode_merge_kernel, static_cast<const float*>(p.ws_acc),
                            static_cast<const float*>(p.ws_ml), p.o, lens, slot_ids, n_slots,
-                           bt_stride, S, H_Q);
+                           bt_stride, S, H_Q, rope != nullptr ? 1 : 0);
     if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
   }
   return CIE_OK;
@@ -552,23 +672,29 @@ size_t cie_decode_workspace_bytes(int batch, int num_q_heads, int head_dim, int 
   return rows * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
 }
 
-int cie_decode_attention(const void* q, const void* k, const void* v, const int64_t* lens,
-                         const int64_t* slot_ids, const int64_t* block_table, void* o,
-                         void* workspace, size_t workspace_bytes, int batch, int num_q_heads,
-                         int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
-                         int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
-                         int64_t kv_head_stride, int num_splits, cie_stream_t stream) {
-  using namespace cie;
+}  // extern "C"
+
+namespace cie {
+namespace decode {
+
+// Shared argument checks and dispatch of the two decode entry points; q is
+// null exactly when `rope` is given.
+int entry(const void* q, const void* k, const void* v, const int64_t* lens,
+          const int64_t* slot_ids, const int64_t* block_table, void* o, void* workspace,
+          size_t workspace_bytes, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+          int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+          int64_t kv_page_stride, int64_t kv_head_stride, int num_splits, cie_stream_t stream,
+          const FusedRope* rope) {
   if (batch < 0) return fail(CIE_ERR_INVALID_ARGUMENT, "batch < 0");
   if (batch == 0) return CIE_OK;
-  if (!q || !k || !v || !lens || !slot_ids || !block_table || !o)
+  if ((!q && !rope) || !k || !v || !lens || !slot_ids || !block_table || !o)
     return fail(CIE_ERR_INVALID_ARGUMENT, "null pointer argument");
-  if (head_dim != decode::kD || page_size != decode::kPage)
+  if (head_dim != kD || page_size != kPage)
     return fail(CIE_ERR_UNSUPPORTED, "head_dim %d / page_size %d (supported: 64 / 16)", head_dim,
                 page_size);
   if (num_kv_heads != 1 && num_kv_heads != 2 && num_kv_heads != 4)
     return fail(CIE_ERR_UNSUPPORTED, "num_kv_heads %d (supported: 1, 2, 4)", num_kv_heads);
-  if (num_q_heads != num_kv_heads * decode::kGroup)
+  if (num_q_heads != num_kv_heads * kGroup)
     return fail(CIE_ERR_UNSUPPORTED, "num_q_heads %d must be 7 * num_kv_heads", num_q_heads);
   if (n_pages < 1 || n_slots < 1 || bt_stride < 1)
     return fail(CIE_ERR_INVALID_ARGUMENT, "n_pages / n_slots / bt_stride must be >= 1");
@@ -579,8 +705,18 @@ int cie_decode_attention(const void* q, const void* k, const void* v, const int6
     return fail(CIE_ERR_INVALID_ARGUMENT, "overlapping K/V strides (page %lld, head %lld)",
                 (long long)kv_page_stride, (long long)kv_head_stride);
   if ((kv_page_stride % 8) || (kv_head_stride % 8) || !aligned16(k) || !aligned16(v) ||
-      !aligned16(q) || !aligned16(o))
+      (q && !aligned16(q)) || !aligned16(o))
     return fail(CIE_ERR_ALIGNMENT, "q/o/k/v must be 16-byte aligned with 16-byte strides");
+  if (rope) {
+    if (!rope->qkv || !rope->cos || !rope->sin)
+      return fail(CIE_ERR_INVALID_ARGUMENT, "null qkv / cos / sin");
+    if (rope->qkv_tok < static_cast<int64_t>(num_q_heads + 2 * num_kv_heads) * head_dim ||
+        rope->cs_tok < head_dim)
+      return fail(CIE_ERR_INVALID_ARGUMENT, "qkv / cos / sin rows overlap");
+    if ((rope->qkv_tok % 8) || (rope->cs_tok % 8) || !aligned16(rope->qkv) ||
+        !aligned16(rope->cos) || !aligned16(rope->sin))
+      return fail(CIE_ERR_ALIGNMENT, "qkv / cos / sin rows must start on 16-byte boundaries");
+  }
   int S = num_splits > 0 ? num_splits : cie_decode_default_splits(batch, current_device());
   if (S > 4096) return fail(CIE_ERR_INVALID_ARGUMENT, "num_splits %d > 4096", S);
   float* ws = nullptr;
@@ -595,15 +731,47 @@ int cie_decode_attention(const void* q, const void* k, const void* v, const int6
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (num_kv_heads) {
     case 1:
-      return decode::launch<1>(q, k, v, lens, slot_ids, block_table, o, ws, batch, n_pages, n_slots,
-                               bt_stride, kv_page_stride, kv_head_stride, S, s);
+      return launch<1>(q, k, v, lens, slot_ids, block_table, o, ws, batch, n_pages, n_slots,
+                       bt_stride, kv_page_stride, kv_head_stride, S, s, rope);
     case 2:
-      return decode::launch<2>(q, k, v, lens, slot_ids, block_table, o, ws, batch, n_pages, n_slots,
-                               bt_stride, kv_page_stride, kv_head_stride, S, s);
+      return launch<2>(q, k, v, lens, slot_ids, block_table, o, ws, batch, n_pages, n_slots,
+                       bt_stride, kv_page_stride, kv_head_stride, S, s, rope);
     default:
-      return decode::launch<4>(q, k, v, lens, slot_ids, block_table, o, ws, batch, n_pages, n_slots,
-                               bt_stride, kv_page_stride, kv_head_stride, S, s);
+      return launch<4>(q, k, v, lens, slot_ids, block_table, o, ws, batch, n_pages, n_slots,
+                       bt_stride, kv_page_stride, kv_head_stride, S, s, rope);
   }
+}
+
+}  // namespace decode
+}  // namespace cie
+
+extern "C" {
+
+int cie_decode_attention(const void* q, const void* k, const void* v, const int64_t* lens,
+                         const int64_t* slot_ids, const int64_t* block_table, void* o,
+                         void* workspace, size_t workspace_bytes, int batch, int num_q_heads,
+                         int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
+                         int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
+                         int64_t kv_head_stride, int num_splits, cie_stream_t stream) {
+  return cie::decode::entry(q, k, v, lens, slot_ids, block_table, o, workspace, workspace_bytes,
+                            batch, num_q_heads, num_kv_heads, head_dim, page_size, n_pages,
+                            n_slots, bt_stride, kv_page_stride, kv_head_stride, num_splits, stream,
+                            nullptr);
+}
+
+int cie_rope_kv_decode_attention(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                                 const void* sin, int64_t cs_tok_stride, void* k_cache,
+                                 void* v_cache, const int64_t* lens, const int64_t* slot_ids,
+                                 const int64_t* block_table, void* o, void* workspace,
+                                 size_t workspace_bytes, int batch, int num_q_heads,
+                                 int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
+                                 int64_t n_slots, int64_t bt_stride, int64_t cache_page_stride,
+                                 int64_t cache_head_stride, int num_splits, cie_stream_t stream) {
+  const cie::decode::FusedRope rope{qkv, qkv_tok_stride, cos, sin, cs_tok_stride};
+  return cie::decode::entry(nullptr, k_cache, v_cache, lens, slot_ids, block_table, o, workspace,
+                            workspace_bytes, batch, num_q_heads, num_kv_heads, head_dim,
+                            page_size, n_pages, n_slots, bt_stride, cache_page_stride,
+                            cache_head_stride, num_splits, stream, &rope);
 }
 
 }  // extern "C"

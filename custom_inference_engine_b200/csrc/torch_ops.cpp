@@ -271,6 +271,45 @@ at::Tensor rope_kv_mixed_update(const at::Tensor& qkv, const at::Tensor& cos,
   return q;
 }
 
+at::Tensor rope_kv_decode_attention(const at::Tensor& qkv, const at::Tensor& cos,
+                                    const at::Tensor& sin, at::Tensor& k_cache,
+                                    at::Tensor& v_cache, const at::Tensor& lens,
+                                    const at::Tensor& slot_ids, const at::Tensor& block_table) {
+  check_rope_src(qkv, cos, sin, k_cache, v_cache);
+  check_i64(lens, "lens");
+  check_i64(slot_ids, "slot_ids");
+  check_i64(block_table, "block_table");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.stride(1) == 1 &&
+                  block_table.size(1) == k_cache.size(0),
+              "block_table must be (n_slots, n_pages)");
+  TORCH_CHECK(slot_ids.dim() == 1 && slot_ids.size(0) == qkv.size(1), "one token per slot id");
+  TORCH_CHECK(lens.dim() == 1 && lens.is_contiguous() && slot_ids.is_contiguous(),
+              "lens (per slot) / slot_ids must be contiguous 1-D");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  at::Tensor o = rope_out(qkv, k_cache);
+  const int64_t B = slot_ids.size(0);
+  if (B == 0) return o;
+  const int hq = static_cast<int>(o.size(2));
+  const int S = cie_decode_default_splits(static_cast<int>(B), qkv.get_device());
+  const size_t ws_bytes = cie_decode_workspace_bytes(static_cast<int>(B), hq,
+                                                     static_cast<int>(k_cache.size(3)), S);
+  at::Tensor ws;
+  if (ws_bytes > 0)
+    ws = at::empty({static_cast<int64_t>(ws_bytes / sizeof(float))}, qkv.options().dtype(at::kFloat));
+  const int st = cie_rope_kv_decode_attention(
+      qkv.data_ptr(), qkv.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1),
+      k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr<int64_t>(),
+      slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(), o.data_ptr(),
+      ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, static_cast<int>(B), hq,
+      static_cast<int>(k_cache.size(1)), static_cast<int>(k_cache.size(3)),
+      static_cast<int>(k_cache.size(2)), k_cache.size(0),
+      lens.size(0) < block_table.size(0) ? lens.size(0) : block_table.size(0),
+      block_table.stride(0), k_cache.stride(0), k_cache.stride(1), S,
+      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "rope_kv_decode_attention");
+  return o;
+}
+
 // ---- Qwen2 body helpers (cie_model_ops.h) ----------------------------------
 
 void check_rows(const at::Tensor& t, const char* name) {
@@ -360,6 +399,9 @@ TORCH_LIBRARY(inference, m) {
   m.def(
       "rope_kv_mixed_update(Tensor qkv, Tensor cos, Tensor sin, Tensor(a!) k_cache, "
       "Tensor(b!) v_cache, Tensor pages, Tensor offsets) -> Tensor");
+  m.def(
+      "rope_kv_decode_attention(Tensor qkv, Tensor cos, Tensor sin, Tensor(a!) k_cache, "
+      "Tensor(b!) v_cache, Tensor lens, Tensor slot_ids, Tensor block_table) -> Tensor");
   m.def("rms_norm(Tensor x, Tensor weight, float eps) -> Tensor");
   m.def("add_rms_norm(Tensor(a!) residual, Tensor delta, Tensor weight, float eps) -> Tensor");
   m.def("silu_and_mul(Tensor gate_up) -> Tensor");
@@ -373,6 +415,7 @@ TORCH_LIBRARY_IMPL(inference, CUDA, m) {
   m.impl("kv_mixed_update", &kv_mixed_update);
   m.impl("rope_kv_decode_update", &rope_kv_decode_update);
   m.impl("rope_kv_mixed_update", &rope_kv_mixed_update);
+  m.impl("rope_kv_decode_attention", &rope_kv_decode_attention);
   m.impl("rms_norm", &rms_norm);
   m.impl("add_rms_norm", &add_rms_norm);
   m.impl("silu_and_mul", &silu_and_mul);

@@ -59,6 +59,10 @@ SIGNATURES = {
     "cie_rope_kv_mixed_update": (c_int, [c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr,
                                          c_ptr, c_ptr, c_i64, c_int, c_int, c_int, c_int, c_i64,
                                          c_i64, c_i64, c_ptr]),
+    "cie_rope_kv_decode_attention": (c_int, [c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr,
+                                             c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_int,
+                                             c_int, c_int, c_int, c_int, c_i64, c_i64, c_i64,
+                                             c_i64, c_i64, c_int, c_ptr]),
     # include/cie_model_ops.h
     "cie_rms_norm": (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_int, c_i64, c_i64, c_i64,
                              ctypes.c_float, c_ptr]),
@@ -159,6 +163,10 @@ def _register_fakes() -> None:
 
     @torch.library.register_fake("inference::rope_kv_mixed_update")
     def _rope_mix_fake(qkv, cos, sin, k_cache, v_cache, pages, offsets):
+        return _rope_out(qkv, k_cache)
+
+    @torch.library.register_fake("inference::rope_kv_decode_attention")
+    def _rope_dec_attn_fake(qkv, cos, sin, k_cache, v_cache, lens, slot_ids, block_table):
         return _rope_out(qkv, k_cache)
 
     @torch.library.register_fake("inference::rms_norm")

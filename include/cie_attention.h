@@ -5,8 +5,9 @@
  * Every entry point takes plain device pointers, sizes and strides (in
  * elements), launches asynchronously on `stream`, performs no host<->device
  * synchronisation and allocates nothing. cie_decode_attention,
- * cie_mixed_attention, cie_kv_decode_update, cie_kv_mixed_update and the two
- * cie_rope_kv_*_update entry points can be captured in a CUDA graph. Return value: CIE_OK or a negative cie_status; on
+ * cie_mixed_attention, cie_kv_decode_update, cie_kv_mixed_update, the two
+ * cie_rope_kv_*_update entry points and cie_rope_kv_decode_attention can be
+ * captured in a CUDA graph. Return value: CIE_OK or a negative cie_status; on
  * error nothing was launched and cie_last_error_message() (thread-local) says
  * why.
  *
@@ -227,6 +228,32 @@ int cie_rope_kv_mixed_update(const void* qkv, int64_t qkv_tok_stride, const void
                              int64_t num_tokens, int num_q_heads, int num_kv_heads, int head_dim,
                              int page_size, int64_t n_pages, int64_t cache_page_stride,
                              int64_t cache_head_stride, cie_stream_t stream);
+
+/* ---- rotary embedding + KV write + decode attention in one launch ---------- */
+
+/*
+ * The whole attention step of a decode pass after the fused QKV projection
+ * (attn/core.py:193-215 of the reference: apply_rotary_pos_emb, then
+ * KVStorage.decode_update, kv_cache/storage.py:87-122, then the decode
+ * attention op): token i (slot s = slot_ids[i], position lens[s], the slot's
+ * length BEFORE it) has its q rotated in registers, its rotated k and plain v
+ * written to page block_table[s * bt_stride + lens[s] / page_size], row
+ * lens[s] % page_size, and attends to the lens[s] + 1 keys of its slot,
+ * itself included. qkv / cos / sin as for cie_rope_kv_decode_update; o as
+ * for cie_decode_attention; `lens` is per SLOT (n_slots entries, as
+ * KVStorage.lens) and is not advanced. Same results, bit for bit, as
+ * cie_rope_kv_decode_update followed by cie_decode_attention with
+ * lens[slot_ids] + 1; workspace as for cie_decode_attention. num_kv_heads
+ * 1, 2 or 4.
+ */
+int cie_rope_kv_decode_attention(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                                 const void* sin, int64_t cs_tok_stride, void* k_cache,
+                                 void* v_cache, const int64_t* lens, const int64_t* slot_ids,
+                                 const int64_t* block_table, void* o, void* workspace,
+                                 size_t workspace_bytes, int batch, int num_q_heads,
+                                 int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
+                                 int64_t n_slots, int64_t bt_stride, int64_t cache_page_stride,
+                                 int64_t cache_head_stride, int num_splits, cie_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -117,3 +117,46 @@ def test_bad_page_is_reported_not_written(cuda_device):
     cabi.rope_kv_mixed_update(qkv, cos, sin, kc, vc, pages, offsets)
     assert native.device_errors(0, clear=True) & 4  # CIE_DEVERR_BAD_PAGE
     assert not torch.equal(kc[3, :, 0], k_cache[3, :, 0])  # the good row was written
+
+
+@pytest.mark.parametrize("splits", [0, 1, 3, 16])
+def test_rope_kv_decode_attention_one_launch(splits, cuda_device):
+    """RoPE + K/V write + decode attention in one launch gives the bits of the
+    two-launch sequence (cie_rope_kv_decode_update, then cie_decode_attention
+    over lens[slot] + 1 keys): the same output and the same pages. Positions
+    cover the first row of a page, the last row, a page boundary, a
+    one-token history and a padding row on slot 0."""
+    dev = cuda_device
+    g = torch.Generator(device=dev).manual_seed(100 + splits)
+    n_slots = 9
+    per_slot = 40                                     # pages per slot: up to 640 tokens
+    n_pages = 1 + (n_slots - 1) * per_slot
+    k0 = torch.randn(n_pages, HKV, PAGE, D, generator=g, device=dev).half()
+    v0 = torch.randn(n_pages, HKV, PAGE, D, generator=g, device=dev).half()
+    perm = torch.randperm(n_pages - 1, generator=torch.Generator().manual_seed(splits)) + 1
+    bt = torch.zeros(n_slots, n_pages, dtype=torch.long)
+    for s in range(1, n_slots):
+        bt[s, :per_slot] = perm[(s - 1) * per_slot:s * per_slot]
+    bt = bt.to(dev)
+    lens = torch.tensor([0, 0, 15, 16, 31, 100, 1, 639, 47], dtype=torch.long, device=dev)
+    slots = torch.tensor([2, 3, 4, 5, 6, 7, 8, 1, 0], dtype=torch.long, device=dev)
+    B = slots.shape[0]
+    wide = (torch.randn(1, B, (HQ + 2 * HKV) * D + 64, generator=g, device=dev) * 3).half()
+    qkv = wide[..., 64:]
+    cos, sin = _rope_tables(lens[slots].tolist(), dev)
+    # two launches
+    k1, v1 = k0.clone(), v0.clone()
+    q = cabi.rope_kv_decode_update(qkv, cos, sin, k1, v1, lens, slots, bt)
+    o_two = cabi.decode_attention(q, k1, v1, lens[slots] + 1, slots, bt, num_splits=splits)
+    # one launch
+    k2, v2 = k0.clone(), v0.clone()
+    o_one = cabi.rope_kv_decode_attention(qkv, cos, sin, k2, v2, lens, slots, bt,
+                                          num_splits=splits)
+    torch.cuda.synchronize()
+    assert torch.equal(o_one, o_two)
+    assert torch.equal(k2[1:], k1[1:]) and torch.equal(v2[1:], v1[1:])
+    # the torch op (default splits) agrees
+    if splits == 0:
+        k3, v3 = k0.clone(), v0.clone()
+        o_op = torch.ops.inference.rope_kv_decode_attention(qkv, cos, sin, k3, v3, lens, slots, bt)
+        assert torch.equal(o_op, o_two) and torch.equal(k3[1:], k1[1:])
