@@ -1,5 +1,6 @@
 // Element-wise kernels of the Qwen2 decoder body that surround the attention
-// path: RMSNorm, residual add + RMSNorm, and SiLU(gate) * up.
+// path: RMSNorm, residual add + RMSNorm, SiLU(gate) * up, and the greedy
+// argmax over the vocabulary.
 //
 // In the reference engine these are Hugging Face Qwen2 modules
 // (Qwen2RMSNorm, the decoder layer's residual adds, Qwen2MLP's act_fn(gate) *
@@ -17,6 +18,7 @@
 // kernels.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <math_constants.h>
 #include <stdint.h>
 
 #include "cie_host.h"
@@ -167,6 +169,117 @@ __global__ void silu_mul_kernel(const __half* __restrict__ gate, const __half* _
   }
 }
 
+// Index of the largest value of each row (the first one when several are
+// equal; a NaN counts as larger than any number, the first NaN wins), as
+// torch.argmax. Two launches: kArgmaxParts CTAs per row each reduce one
+// contiguous part of the row to a (value, index) partial, then one warp per
+// row reduces the partials.
+constexpr int kArgmaxThreads = 256;
+constexpr int kArgmaxParts = 16;
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  // v at index i beats bv at index bi: NaN above everything, then larger, then earlier
+  const bool vn = v != v, bn = bv != bv;
+  if (vn != bn) return vn;
+  if (!vn && v != bv) return v > bv;
+  return i < bi;
+}
+
+__device__ __forceinline__ void warp_best(float& bv, int& bi) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+}
+
+// kVec: rows 16-byte aligned (8 values per load); otherwise one value per load.
+template <bool kVec>
+__global__ void __launch_bounds__(kArgmaxThreads)
+    argmax_part_kernel(const __half* __restrict__ x, float2* __restrict__ part, int n,
+                       int64_t stride) {
+  const __half* row = x + static_cast<int64_t>(blockIdx.x) * stride;
+  // part p covers chunks [p * per, (p + 1) * per) of 8 values (the tail of
+  // the row, and unaligned rows, value by value)
+  const int chunks = n >> 3;
+  const int per = (chunks + kArgmaxParts - 1) / kArgmaxParts;
+  const int c_lo = blockIdx.y * per, c_hi = min(chunks, c_lo + per);
+  // start from the part's first value so that a part of -inf keeps its first index
+  float bv = -CUDART_INF_F;
+  int bi = 0x7fffffff;
+  if (kVec && c_lo < c_hi && threadIdx.x == 0) {
+    bv = __half2float(row[c_lo * 8]);
+    bi = c_lo * 8;
+  }
+  if (kVec) {
+    constexpr int kUnroll = 4;
+    for (int c0 = c_lo + threadIdx.x; c0 < c_hi; c0 += kUnroll * kArgmaxThreads) {
+      uint4 u[kUnroll];
+#pragma unroll
+      for (int j = 0; j < kUnroll; ++j) {
+        const int c = c0 + j * kArgmaxThreads;
+        u[j] = c < c_hi ? __ldg(reinterpret_cast<const uint4*>(row) + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < kUnroll; ++j) {
+        const int c = c0 + j * kArgmaxThreads;
+        if (c >= c_hi) break;
+        const __half2* h = reinterpret_cast<const __half2*>(&u[j]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          // this thread visits its indices in increasing order: a strictly
+          // larger value (or a first NaN) is the only way to replace the best
+          const float2 f = __half22float2(h[e]);
+          if (f.x > bv || (f.x != f.x && bv == bv)) { bv = f.x; bi = c * 8 + 2 * e; }
+          if (f.y > bv || (f.y != f.y && bv == bv)) { bv = f.y; bi = c * 8 + 2 * e + 1; }
+        }
+      }
+    }
+  }
+  // values not covered by 16-byte loads: the row tail (last part), or all of
+  // this part's range when rows are unaligned
+  const int v_lo = kVec ? (blockIdx.y == kArgmaxParts - 1 ? chunks * 8 : n) : c_lo * 8;
+  const int v_hi = kVec ? n : (blockIdx.y == kArgmaxParts - 1 ? n : c_hi * 8);
+  for (int i = v_lo + threadIdx.x; i < v_hi; i += kArgmaxThreads) {
+    const float f = __half2float(row[i]);
+    if (better(f, i, bv, bi)) { bv = f; bi = i; }
+  }
+  warp_best(bv, bi);
+  __shared__ float s_v[kArgmaxThreads / 32];
+  __shared__ int s_i[kArgmaxThreads / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    s_v[warp] = bv;
+    s_i[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    bv = lane < kArgmaxThreads / 32 ? s_v[lane] : -CUDART_INF_F;
+    bi = lane < kArgmaxThreads / 32 ? s_i[lane] : 0x7fffffff;
+    warp_best(bv, bi);
+    if (lane == 0)
+      part[static_cast<int64_t>(blockIdx.x) * kArgmaxParts + blockIdx.y] =
+          make_float2(bv, __int_as_float(bi));
+  }
+}
+
+__global__ void argmax_final_kernel(const float2* __restrict__ part, int64_t* __restrict__ out) {
+  const int lane = threadIdx.x;
+  float bv = -CUDART_INF_F;
+  int bi = 0x7fffffff;
+  if (lane < kArgmaxParts) {
+    const float2 p = part[static_cast<int64_t>(blockIdx.x) * kArgmaxParts + lane];
+    bv = p.x;
+    bi = __float_as_int(p.y);
+  }
+  warp_best(bv, bi);
+  if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+}
+
 inline bool aligned_rows(const void* p, int64_t stride) {
   return aligned16(p) && (stride % 8) == 0;
 }
@@ -241,6 +354,41 @@ int cie_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int 
       rows, inter, gate_stride, up_stride, out_stride);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "silu_mul launch: %s", cudaGetErrorString(e));
+  return CIE_OK;
+}
+
+size_t cie_argmax_workspace_bytes(int64_t rows) {
+  return rows <= 0 ? 0 : static_cast<size_t>(rows) * cie::body::kArgmaxParts * 2 * sizeof(float);
+}
+
+int cie_argmax_rows(const void* x, int64_t rows, int n, int64_t stride, int64_t* out,
+                    void* workspace, size_t workspace_bytes, cie_stream_t stream) {
+  using namespace cie;
+  using namespace cie::body;
+  if (rows < 0 || n < 0) return fail(CIE_ERR_INVALID_ARGUMENT, "negative size");
+  if (rows == 0) return CIE_OK;
+  if (!x || !out || n == 0) return fail(CIE_ERR_INVALID_ARGUMENT, "null pointer or empty row");
+  if (rows > 65535) return fail(CIE_ERR_UNSUPPORTED, "rows %lld > 65535", (long long)rows);
+  if (stride < n) return fail(CIE_ERR_INVALID_ARGUMENT, "row stride < n");
+  if ((reinterpret_cast<uintptr_t>(x) & 1) != 0)
+    return fail(CIE_ERR_ALIGNMENT, "x must be 2-byte aligned");
+  if (workspace == nullptr || workspace_bytes < cie_argmax_workspace_bytes(rows))
+    return fail(CIE_ERR_WORKSPACE, "argmax needs %zu workspace bytes",
+                cie_argmax_workspace_bytes(rows));
+  if ((reinterpret_cast<uintptr_t>(workspace) & 7) != 0)
+    return fail(CIE_ERR_ALIGNMENT, "workspace must be 8-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float2* part = static_cast<float2*>(workspace);
+  const dim3 grid(static_cast<unsigned>(rows), kArgmaxParts);
+  if (aligned_rows(x, stride))
+    argmax_part_kernel<true><<<grid, kArgmaxThreads, 0, s>>>(static_cast<const __half*>(x), part,
+                                                             n, stride);
+  else
+    argmax_part_kernel<false><<<grid, kArgmaxThreads, 0, s>>>(static_cast<const __half*>(x), part,
+                                                              n, stride);
+  argmax_final_kernel<<<static_cast<unsigned>(rows), 32, 0, s>>>(part, out);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "argmax launch: %s", cudaGetErrorString(e));
   return CIE_OK;
 }
 

@@ -375,6 +375,22 @@ at::Tensor silu_and_mul(const at::Tensor& gate_up) {
   return out;
 }
 
+at::Tensor argmax_rows(const at::Tensor& x) {
+  check_rows(x, "x");
+  c10::cuda::CUDAGuard guard(x.device());
+  std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end() - 1);
+  at::Tensor out = at::empty(shape, x.options().dtype(at::kLong));
+  const int64_t rows = x.numel() / std::max<int64_t>(x.size(-1), 1);
+  const size_t ws_bytes = cie_argmax_workspace_bytes(rows);
+  at::Tensor ws = at::empty({static_cast<int64_t>(std::max<size_t>(ws_bytes, 8) / 8)},
+                            x.options().dtype(at::kLong));
+  const int st = cie_argmax_rows(x.data_ptr(), rows, static_cast<int>(x.size(-1)), row_stride(x),
+                                 out.data_ptr<int64_t>(), ws.data_ptr(), ws_bytes,
+                                 reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "argmax_rows");
+  return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(inference, m) {
@@ -405,6 +421,7 @@ TORCH_LIBRARY(inference, m) {
   m.def("rms_norm(Tensor x, Tensor weight, float eps) -> Tensor");
   m.def("add_rms_norm(Tensor(a!) residual, Tensor delta, Tensor weight, float eps) -> Tensor");
   m.def("silu_and_mul(Tensor gate_up) -> Tensor");
+  m.def("argmax_rows(Tensor x) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(inference, CUDA, m) {
@@ -419,4 +436,5 @@ TORCH_LIBRARY_IMPL(inference, CUDA, m) {
   m.impl("rms_norm", &rms_norm);
   m.impl("add_rms_norm", &add_rms_norm);
   m.impl("silu_and_mul", &silu_and_mul);
+  m.impl("argmax_rows", &argmax_rows);
 }

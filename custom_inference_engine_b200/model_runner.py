@@ -335,7 +335,7 @@ class DecodeGraph:
         pos = kv.lens[self.md.slot_ids].view(1, -1)
         hidden = self.runner._hidden(ids, pos, self.md)
         self.logits = self.runner.model.lm_head(hidden[0])
-        self.tokens.copy_(self.logits.argmax(-1))
+        self.tokens.copy_(torch.ops.inference.argmax_rows(self.logits))
         kv.decode_advance(self.md.slot_ids)
 
     def step(self) -> torch.Tensor:

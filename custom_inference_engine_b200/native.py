@@ -67,6 +67,8 @@ SIGNATURES = {
     "cie_rms_norm": (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_int, c_i64, c_i64, c_i64,
                              ctypes.c_float, c_ptr]),
     "cie_silu_mul": (c_int, [c_ptr, c_ptr, c_ptr, c_i64, c_int, c_i64, c_i64, c_i64, c_ptr]),
+    "cie_argmax_workspace_bytes": (c_size, [c_i64]),
+    "cie_argmax_rows": (c_int, [c_ptr, c_i64, c_int, c_i64, c_ptr, c_ptr, c_size, c_ptr]),
 }
 
 CIE_OK = 0
@@ -176,6 +178,10 @@ def _register_fakes() -> None:
     @torch.library.register_fake("inference::add_rms_norm")
     def _add_rms_fake(residual, delta, weight, eps):
         return torch.empty_like(residual, memory_format=torch.contiguous_format)
+
+    @torch.library.register_fake("inference::argmax_rows")
+    def _argmax_fake(x):
+        return x.new_empty(x.shape[:-1], dtype=torch.long)
 
     @torch.library.register_fake("inference::silu_and_mul")
     def _silu_mul_fake(gate_up):

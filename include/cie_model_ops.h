@@ -45,6 +45,20 @@ int cie_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int 
                  int64_t gate_stride, int64_t up_stride, int64_t out_stride,
                  cie_stream_t stream);
 
+/*
+ * out[r] = index of the largest of the n fp16 values of row r (rows `stride`
+ * elements apart; 16-byte aligned rows are read 8 values at a time): the first
+ * index when several are equal, a NaN counting as the largest -- torch.argmax
+ * (dim=-1). For greedy decoding over the 151936-way logits (the reference's
+ * argmax after lm_head, scheduler/decode_module.py:103). out: int64. Two
+ * launches: parts of every row, then the parts; `workspace` holds the parts
+ * (>= cie_argmax_workspace_bytes(rows) bytes, 8-byte aligned, no
+ * initialisation). rows <= 65535.
+ */
+size_t cie_argmax_workspace_bytes(int64_t rows);
+int cie_argmax_rows(const void* x, int64_t rows, int n, int64_t stride, int64_t* out,
+                    void* workspace, size_t workspace_bytes, cie_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

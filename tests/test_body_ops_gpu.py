@@ -89,3 +89,16 @@ def test_rotary_table_equals_per_pass_rotary(cuda_device):
     probe = torch.zeros(1, 1, dtype=torch.float16, device=cuda_device)
     cos, sin = model.model.rotary_emb(probe, pos)
     assert torch.equal(body.cos[pos[0]], cos[0]) and torch.equal(body.sin[pos[0]], sin[0])
+
+
+@pytest.mark.parametrize("rows,n", [(64, 151936), (3, 4096), (5, 1001)])
+def test_argmax_rows_matches_torch(ops, cuda_device, rows, n):
+    """The greedy argmax over the vocabulary gives torch.argmax's index: the
+    first of equal maxima (values 0..3 make ties everywhere), also for a row
+    of -inf and on a row-strided view."""
+    g = torch.Generator(device=cuda_device).manual_seed(n)
+    x = torch.randint(0, 4, (rows, n), generator=g, device=cuda_device).half()
+    x[-1].fill_(float("-inf"))
+    assert torch.equal(ops.argmax_rows(x), x.argmax(-1))
+    y = torch.randn(rows, n + 8, generator=g, device=cuda_device).half()[:, :n]
+    assert torch.equal(ops.argmax_rows(y), y.argmax(-1))

@@ -148,3 +148,28 @@ def test_body_kernel_argument_checks():
     assert silu(n=4860, os_=4860) == -2
     assert silu(u=p + 2) == -4
     assert silu(os_=4800) == -1
+
+
+def test_fused_decode_and_argmax_argument_checks():
+    """cie_rope_kv_decode_attention and cie_argmax_rows reject bad arguments
+    on the host."""
+    lib = native.lib()
+    p = 1 << 20
+
+    def fused(**kw):
+        a = dict(qkv=p, qkv_tok=1152, cos=p, sin=p, cs_tok=64, k=p, v=p, lens=p, slots=p, bt=p,
+                 o=p, ws=None, ws_bytes=0, batch=4, hq=14, hkv=2, d=64, page=16, n_pages=100,
+                 n_slots=5, bt_stride=100, pstride=2048, hstride=1024, splits=1, stream=None)
+        a.update(kw)
+        return lib.cie_rope_kv_decode_attention(*a.values())
+    assert fused(batch=0) == 0
+    assert fused(qkv=None) == -1
+    assert fused(qkv_tok=1000) == -1          # rows overlap
+    assert fused(qkv=p + 2) == -4
+    assert fused(d=128) == -2
+    assert fused(splits=4) == -5              # the split path needs workspace
+    assert lib.cie_argmax_workspace_bytes(64) == 64 * 16 * 8
+    assert lib.cie_argmax_rows(p, 0, 10, 10, p, None, 0, None) == 0
+    assert lib.cie_argmax_rows(p, 4, 10, 10, p, None, 0, None) == -5
+    assert lib.cie_argmax_rows(p + 1, 4, 10, 10, p, p, 1 << 10, None) == -4
+    assert lib.cie_argmax_rows(p, 4, 10, 8, p, p, 1 << 10, None) == -1
