@@ -19,5 +19,6 @@ from .attention import (  # noqa: F401
     mixed_attention_blockwise,
     mixed_attention_fp32,
     mixed_update_ref,
+    rope_ref,
     valid_token_rows,
 )

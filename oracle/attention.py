@@ -16,6 +16,8 @@ Two families of functions live here:
   (``tests/golden/make_golden.py``) and documents exactly what rounding the
   reference performs.
 * ``*_update_ref``: the KV-page scatter, bit-exact.
+* ``rope_ref``: the rotary embedding the reference applies to q and k
+  before the scatter, in fp16 as its torch ops round.
 
 All citations are ``path:line`` inside the reference project
 (eteboun/custom_inference_engine).
@@ -294,3 +296,22 @@ def mixed_update_ref(k_cache, v_cache, pages, offsets, k_proj, v_proj):
     hkv, d = k_cache.shape[1], k_cache.shape[3]
     k_cache[pages, :, offsets] = k_proj.reshape(-1, hkv, d)
     v_cache[pages, :, offsets] = v_proj.reshape(-1, hkv, d)
+
+
+# --------------------------------------------------------------------------
+# rotary embedding before the scatter
+# --------------------------------------------------------------------------
+
+def rope_ref(x, cos, sin):
+    """The rotary embedding of ``x`` (1, T, H, D) fp16 with per-token tables
+    ``cos`` / ``sin`` (1, T, D) fp16, as the reference applies it to the
+    split QKV projection before the KV write (attn/core.py:193-198, through
+    transformers' Qwen2 ``apply_rotary_pos_emb`` with ``unsqueeze_dim=2``):
+    ``x * cos + rotate_half(x) * sin`` where ``rotate_half`` maps the halves
+    (x1, x2) to (-x2, x1). Every op rounds to fp16 the way torch's half
+    arithmetic does (product, product, sum)."""
+    c = cos.unsqueeze(2)
+    s = sin.unsqueeze(2)
+    half = x.shape[-1] // 2
+    rot = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return x * c + rot * s

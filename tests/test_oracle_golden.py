@@ -104,3 +104,22 @@ def test_mixed_update_oracle_bit_exact():
     oracle.mixed_update_ref(k, v, g["pages"], g["offsets"], k_proj, v_proj)
     assert torch.equal(k[1:], g["k_after"][1:])
     assert torch.equal(v[1:], g["v_after"][1:])
+
+
+def test_rope_oracle_matches_transformers_bit_exact():
+    """oracle.rope_ref is transformers' Qwen2 apply_rotary_pos_emb (the
+    function the reference calls, attn/core.py:193-198) bit for bit on fp16
+    CPU tensors, for q and k head counts, at positions up to 32767."""
+    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
+
+    g = torch.Generator().manual_seed(0)
+    T = 33
+    q = (torch.randn(1, T, 14, 64, generator=g) * 3).half()
+    k = (torch.randn(1, T, 2, 64, generator=g) * 3).half()
+    pos = torch.randint(0, 32768, (T,), generator=g).float()
+    inv = 1.0 / (1e6 ** (torch.arange(0, 64, 2).float() / 64))
+    emb = torch.cat((pos[:, None] * inv, pos[:, None] * inv), dim=-1)
+    cos, sin = emb.cos()[None].half(), emb.sin()[None].half()
+    q_hf, k_hf = apply_rotary_pos_emb(q, k, cos, sin, unsqueeze_dim=2)
+    assert torch.equal(oracle.rope_ref(q, cos, sin), q_hf)
+    assert torch.equal(oracle.rope_ref(k, cos, sin), k_hf)
