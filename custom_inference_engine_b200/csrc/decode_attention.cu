@@ -563,6 +563,65 @@ __global__ void __launch_bounds__(256)
       __floats2half2_rn(num.x * inv, num.y * inv);
 }
 
+// Split counts up to this use decode_merge_small_kernel.
+constexpr int kSmallMergeSplits = 8;
+
+// The same combination for S <= kSmallMergeSplits with one CTA per sequence and
+// one warp per query head (lane = two output columns): the warp reads the
+// sequence's active partials at once and folds them in split order. This is
+// the arithmetic and order of decode_merge_kernel for such S (there each split
+// sits in a warp of its own and warp 0 folds them in warp order); the grid is
+// B CTAs instead of H_q x B CTAs of 8 warps, most of which have nothing to
+// fold when S is small.
+__global__ void __launch_bounds__(1024)
+    decode_merge_small_kernel(const float* __restrict__ ws_acc, const float* __restrict__ ws_ml,
+                              __half* __restrict__ o, const int64_t* __restrict__ lens,
+                              const int64_t* __restrict__ slot_ids, int64_t n_slots,
+                              int64_t bt_stride, int num_splits, int num_q_heads,
+                              int lens_per_slot) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int hq = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.x;
+  const int S = num_splits;
+  const int np = seq_pages(lens, slot_ids, b, n_slots, bt_stride, lens_per_slot);
+  const int pps = split_pages(np, S);
+  const int active = np == 0 ? 0 : (np + pps - 1) / pps;
+
+  float m[kSmallMergeSplits], ls[kSmallMergeSplits];
+  float2 a[kSmallMergeSplits];
+#pragma unroll
+  for (int s = 0; s < kSmallMergeSplits; ++s) {
+    if (s < active) {
+      const int64_t r = (static_cast<int64_t>(b) * S + s) * num_q_heads + hq;
+      m[s] = ws_ml[r * 2];   // finite: every active split saw a key
+      ls[s] = ws_ml[r * 2 + 1];
+      a[s] = *reinterpret_cast<const float2*>(ws_acc + r * kD + 2 * lane);
+    } else {
+      m[s] = -CUDART_INF_F;
+      ls[s] = 0.f;
+      a[s] = make_float2(0.f, 0.f);
+    }
+  }
+  float Mt = -CUDART_INF_F;
+#pragma unroll
+  for (int s = 0; s < kSmallMergeSplits; ++s) Mt = fmaxf(Mt, m[s]);
+  float den = 0.f;
+  float2 num = make_float2(0.f, 0.f);
+  if (Mt != -CUDART_INF_F) {
+#pragma unroll
+    for (int s = 0; s < kSmallMergeSplits; ++s) {
+      const float wt = m[s] == -CUDART_INF_F ? 0.f : ex2((m[s] - Mt) * kLog2e);
+      den += wt * ls[s];
+      num.x += wt * a[s].x;
+      num.y += wt * a[s].y;
+    }
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  *reinterpret_cast<__half2*>(o + (static_cast<int64_t>(b) * num_q_heads + hq) * kD + 2 * lane) =
+      __floats2half2_rn(num.x * inv, num.y * inv);
+}
+
 // Arguments of the fused rotary embedding + KV write (see Params).
 struct FusedRope {
   const void* qkv;
@@ -628,9 +687,10 @@ int launch(const void* q, const void* k, const void* v, const int64_t* lens,
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   if (S > 1) {
+    const bool small = S <= kSmallMergeSplits;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(H_Q, batch);
-    cfg.blockDim = dim3(256);
+    cfg.gridDim = small ? dim3(batch) : dim3(H_Q, batch);
+    cfg.blockDim = dim3(small ? 32 * H_Q : 256);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -638,7 +698,8 @@ int launch(const void* q, const void* k, const void* v, const int64_t* lens,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, decode_merge_kernel, static_cast<const float*>(p.ws_acc),
+    e = cudaLaunchKernelEx(&cfg, small ? decode_merge_small_kernel : decode_merge_kernel,
+                           static_cast<const float*>(p.ws_acc),
                            static_cast<const float*>(p.ws_ml), p.o, lens, slot_ids, n_slots,
                            bt_stride, S, H_Q, rope != nullptr ? 1 : 0);
     if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
