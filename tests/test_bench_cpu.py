@@ -59,3 +59,14 @@ def test_reference_arm_two_ranks_rank0_prints():
     lines = _lines(r.stdout)
     assert len(lines) == 1, r.stdout
     _check(lines[0], 2)
+
+
+def test_decode_bytes_is_the_algorithmic_formula():
+    """bench.decode_bytes: K+V rows (512 B per token at 2 kv heads x 64 x fp16,
+    K and V), q and o (14 x 64 fp16 each) and one int64 block-table entry per
+    visited page; 538,312,704 B at the bench point B=256 x 4096."""
+    import bench
+
+    assert bench.decode_bytes(256, 4096) == 538_312_704
+    assert bench.decode_bytes(256, 4096) == 256 * 4096 * 512 + 256 * 3584 + 256 * 256 * 8
+    assert bench.decode_bytes(1, 17) == 17 * 512 + 3584 + 2 * 8
