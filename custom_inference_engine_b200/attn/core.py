@@ -23,16 +23,20 @@ from __future__ import annotations
 
 import torch
 
-from .. import native
+from custom_inference_engine_b200 import native
 
 native.load_ops()
 
-gqa_decode_attention_op = torch.ops.inference.gqa_decode_attention
-gqa_mixed_attention_op = torch.ops.inference.gqa_mixed_attention
-rope_kv_decode_update_op = torch.ops.inference.rope_kv_decode_update
-rope_kv_mixed_update_op = torch.ops.inference.rope_kv_mixed_update
-rope_kv_decode_attention_op = torch.ops.inference.rope_kv_decode_attention
-_gqa_decode_attention_splits = torch.ops.inference.gqa_decode_attention_splits
+# The op OVERLOADS, not the packets: a call through ``torch.ops.inference.X.default``
+# is what Dynamo records as the node target, and the reference's piecewise
+# splitter matches exactly ``torch.ops.inference.gqa_mixed_attention.default``
+# (piecewise/utils.py:5-7), as a ``triton_op`` call in the reference produces.
+gqa_decode_attention_op = torch.ops.inference.gqa_decode_attention.default
+gqa_mixed_attention_op = torch.ops.inference.gqa_mixed_attention.default
+rope_kv_decode_update_op = torch.ops.inference.rope_kv_decode_update.default
+rope_kv_mixed_update_op = torch.ops.inference.rope_kv_mixed_update.default
+rope_kv_decode_attention_op = torch.ops.inference.rope_kv_decode_attention.default
+_gqa_decode_attention_splits = torch.ops.inference.gqa_decode_attention_splits.default
 
 # The reference tunes Triton tiles here (attn/core.py:114-116). The CUDA decode
 # path has one knob, the number of KV splits per sequence; 0 lets the library

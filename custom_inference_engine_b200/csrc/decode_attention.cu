@@ -738,14 +738,15 @@ size_t cie_decode_workspace_bytes(int batch, int num_q_heads, int head_dim, int 
 namespace cie {
 namespace decode {
 
-// Shared argument checks and dispatch of the two decode entry points; q is
-// null exactly when `rope` is given.
-int entry(const void* q, const void* k, const void* v, const int64_t* lens,
-          const int64_t* slot_ids, const int64_t* block_table, void* o, void* workspace,
-          size_t workspace_bytes, int batch, int num_q_heads, int num_kv_heads, int head_dim,
-          int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
-          int64_t kv_page_stride, int64_t kv_head_stride, int num_splits, cie_stream_t stream,
-          const FusedRope* rope) {
+// Argument checks shared by every decode entry point (everything but the
+// workspace); q is null exactly when `rope` is given. On success *splits is
+// the split count the call will use (0 when batch == 0: nothing to do).
+int check_args(const void* q, const void* k, const void* v, const int64_t* lens,
+               const int64_t* slot_ids, const int64_t* block_table, const void* o, int batch,
+               int num_q_heads, int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
+               int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
+               int64_t kv_head_stride, int num_splits, const FusedRope* rope, int* splits) {
+  *splits = 0;
   if (batch < 0) return fail(CIE_ERR_INVALID_ARGUMENT, "batch < 0");
   if (batch == 0) return CIE_OK;
   if ((!q && !rope) || !k || !v || !lens || !slot_ids || !block_table || !o)
@@ -778,8 +779,24 @@ int entry(const void* q, const void* k, const void* v, const int64_t* lens,
         !aligned16(rope->cos) || !aligned16(rope->sin))
       return fail(CIE_ERR_ALIGNMENT, "qkv / cos / sin rows must start on 16-byte boundaries");
   }
-  int S = num_splits > 0 ? num_splits : cie_decode_default_splits(batch, current_device());
+  const int S = num_splits > 0 ? num_splits : cie_decode_default_splits(batch, current_device());
   if (S > 4096) return fail(CIE_ERR_INVALID_ARGUMENT, "num_splits %d > 4096", S);
+  *splits = S;
+  return CIE_OK;
+}
+
+// Argument checks and dispatch of the decode entry points.
+int entry(const void* q, const void* k, const void* v, const int64_t* lens,
+          const int64_t* slot_ids, const int64_t* block_table, void* o, void* workspace,
+          size_t workspace_bytes, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+          int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+          int64_t kv_page_stride, int64_t kv_head_stride, int num_splits, cie_stream_t stream,
+          const FusedRope* rope) {
+  int S = 0;
+  const int st = check_args(q, k, v, lens, slot_ids, block_table, o, batch, num_q_heads,
+                            num_kv_heads, head_dim, page_size, n_pages, n_slots, bt_stride,
+                            kv_page_stride, kv_head_stride, num_splits, rope, &S);
+  if (st != CIE_OK || S == 0) return st;
   float* ws = nullptr;
   if (S > 1) {
     const size_t need = cie_decode_workspace_bytes(batch, num_q_heads, head_dim, S);

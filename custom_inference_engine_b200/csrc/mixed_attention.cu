@@ -877,8 +877,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int cc = 0; cc < kD / 2; ++cc)
             reinterpret_cast<float2*>(rec)[cc] =
                 make_float2(__uint_as_float(ob[cc * 2 + 0]), __uint_as_float(ob[cc * 2 + 1]));
-          rec[kD] = m_ref;
-          rec[kD + 1] = l_run;
+          // a piece whose pipeline wait gave up (ok == false; the device
+          // error bit is set) publishes an empty range, which the merge skips,
+          // instead of whatever its accumulators hold
+          rec[kD] = ok ? m_ref : -CUDART_INF_F;
+          rec[kD + 1] = ok ? l_run : 0.f;
         }
         __threadfence();
         // every working softmax thread of both tiles has published its rows

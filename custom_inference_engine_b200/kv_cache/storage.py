@@ -14,11 +14,11 @@ import math
 
 import torch
 
-from .. import native
+from custom_inference_engine_b200 import native
 
 native.load_ops()
-_decode_update = torch.ops.inference.kv_decode_update
-_mixed_update = torch.ops.inference.kv_mixed_update
+_decode_update = torch.ops.inference.kv_decode_update.default
+_mixed_update = torch.ops.inference.kv_mixed_update.default
 
 
 class KVStorage:

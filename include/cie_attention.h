@@ -107,8 +107,12 @@ int cie_decode_attention(const void* q, const void* k, const void* v, const int6
  * not exceed CIE_DECODE_NOALLOC_SCRATCH_BYTES (4 MiB, i.e. batch x splits <= 1134
  * for 14 heads of 64); larger requests return CIE_ERR_WORKSPACE.
  * Every GPU that loads the library holds the 4 MiB until the process exits.
- * The first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture. All calls
+ * A call outside a stream capture looks up the array's device address (with
+ * the call's device current) and caches it per device; a call whose stream is
+ * capturing uses the cached address, so make the first call on a device before
+ * any stream capture (a first call inside a capture returns
+ * CIE_ERR_INVALID_ARGUMENT). Arguments are checked as cie_decode_attention
+ * checks them, before the scratch limit, with the same status codes. All calls
  * on a device share the array and it keeps the last call's contents (nothing
  * in it needs to start at zero); calls that overlap on the GPU race on it.
  */

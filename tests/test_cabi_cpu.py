@@ -173,3 +173,23 @@ def test_fused_decode_and_argmax_argument_checks():
     assert lib.cie_argmax_rows(p, 4, 10, 10, p, None, 0, None) == -5
     assert lib.cie_argmax_rows(p + 1, 4, 10, 10, p, p, 1 << 10, None) == -4
     assert lib.cie_argmax_rows(p, 4, 10, 8, p, p, 1 << 10, None) == -1
+
+
+def test_noalloc_checks_arguments_before_its_scratch_limit():
+    """cie_decode_attention_noalloc reports a bad argument with the status
+    cie_decode_attention gives it; CIE_ERR_WORKSPACE only for a valid request
+    that is too large for the built-in scratch."""
+    lib = native.lib()
+
+    def noalloc(**kw):
+        a = dict(q=1 << 20, k=1 << 21, v=1 << 22, lens=1 << 23, slot_ids=1 << 24, bt=1 << 25,
+                 o=1 << 26, batch=4, hq=14, hkv=2, d=64, page=16, n_pages=100, n_slots=5,
+                 bt_stride=100, pstride=2048, hstride=1024, splits=1, stream=None)
+        a.update(kw)
+        return lib.cie_decode_attention_noalloc(*a.values())
+    assert noalloc(batch=0) == 0
+    assert noalloc(q=None, splits=5000) == -1      # null pointer, not a scratch overflow
+    assert noalloc(splits=5000) == -1              # num_splits > 4096 is invalid
+    assert noalloc(d=128, splits=400) == -2
+    assert noalloc(k=(1 << 21) + 2, splits=400) == -4
+    assert noalloc(splits=400) == -5               # valid, but 4 x 400 splits > 4 MiB

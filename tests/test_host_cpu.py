@@ -19,7 +19,10 @@ def test_op_schemas_match_the_reference_triton_ops():
                         "Tensor slot_ids, Tensor block_table) -> Tensor")
     upd = torch.ops.inference.kv_decode_update.default._schema
     assert upd.arguments[0].alias_info.is_write and upd.arguments[1].alias_info.is_write
-    assert core.gqa_mixed_attention_op.default is torch.ops.inference.gqa_mixed_attention.default
+    # the module exposes the overloads, which is what a call records as the FX
+    # node target (the reference's piecewise splitter matches this object)
+    assert core.gqa_mixed_attention_op is torch.ops.inference.gqa_mixed_attention.default
+    assert core.gqa_decode_attention_op is torch.ops.inference.gqa_decode_attention.default
 
 
 def test_fake_kernels_propagate_shapes():

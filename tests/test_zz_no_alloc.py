@@ -14,7 +14,6 @@ from custom_inference_engine_b200 import cabi, native
 from custom_inference_engine_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
-TOL = 2e-3
 
 
 def _case(lens, seed, dev):
@@ -23,18 +22,23 @@ def _case(lens, seed, dev):
 
 
 def test_noalloc_matches_workspace_entry_point_twice(cuda_device):
+    """Both entry points launch the same kernels with the same split count, so
+    their outputs are compared bit for bit. The calls run large, small, large:
+    the small call's partials cover only the start of the scratch, with the
+    previous call's partials left beyond them, so a read outside the call's own
+    region would show up as a difference."""
     native.device_errors(0, clear=True)
-    # two different problems back to back: the second call must not see the
-    # first call's leftovers in the shared scratch
-    cases = [(_case([1, 300, 17, 0, 4096, 1024, 33, 2000], 41, cuda_device), 8),
-             (_case([4096] * 3 + [5, 800], 42, cuda_device), 0)]
+    cases = [(_case([4096] * 3 + [5, 800], 42, cuda_device), 0),       # ~59 splits per row
+             (_case([1, 300, 17, 0], 41, cuda_device), 2),
+             (_case([1, 300, 17, 0, 4096, 1024, 33, 2000], 43, cuda_device), 8)]
     for args, splits in cases:
         S = splits or cabi.decode_default_splits(args[4].shape[0], 0)
         assert cabi.decode_workspace_bytes(args[4].shape[0], 14, 64, S) > 0
-        got = cabi.decode_attention_noalloc(*args, num_splits=splits)
-        want = cabi.decode_attention(*args, num_splits=splits)
-        torch.cuda.synchronize()
-        assert (got.float() - want.float()).abs().max().item() <= TOL
+        for _ in range(2):
+            got = cabi.decode_attention_noalloc(*args, num_splits=splits)
+            want = cabi.decode_attention(*args, num_splits=splits)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want)
     assert native.device_errors(0) == 0
 
 
