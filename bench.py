@@ -1,6 +1,6 @@
 """Benchmark of the paged GQA decode-attention hot path on B200.
 
-Default workload (BASELINE config 2's target point): B = 256 sequences x
+Default workload (the B=256 x 4096 decode point): B = 256 sequences x
 kv_len 4096, 14 q / 2 kv heads, head_dim 64, 16-token pages scattered by a
 random permutation over the pool, fp16 N(0, 1) data. One step = one call of
 the decode-attention op over the batch (split-KV load, plus merge when the
@@ -15,15 +15,25 @@ Legs:
             with all inputs resident; inputs (537 MB of K/V) exceed L2. The
             steps run as replays of CUDA graphs of 100 calls each, as the
             engine's captured decode steps do (--eager: Python launches).
-  e2e       the same metric through the C ABI with HOST buffers: every step
-            copies q, the K/V pools, lens, slot ids and the block table from
-            pinned host memory and reads the output back (PCIe-bound: the
-            537 MB pool crosses every step). e2e.resident_pool: the step as
-            the engine runs it, the pool resident in HBM and only the step's
-            q, new K/V rows, lengths and slot ids copied in.
+  e2e       the same metric through the C ABI from HOST buffers, as the
+            engine runs a decode step: the KV pool and block table are the
+            engine's resident state in HBM (copied in once), and every step
+            copies that step's own inputs -- q, the new K/V row of every
+            sequence, the lengths and the slot ids -- from pinned host memory,
+            writes the rows (cie_kv_decode_update), runs cie_decode_attention
+            and reads o back. e2e.full_pool_copy: the whole 537 MB pool and
+            the block table copied from the host every step (PCIe-bound).
   roofline  dominant kernel's achieved algorithmic GB/s / measured HBM peak.
   cpu_baseline  the CPU oracle (torch fp32 gather + softmax) on the host's
             cores over a bounded sample of the same workload.
+  mixed     mixed attention (512-token chunks, config 3): device time, e2e
+            through the C ABI, CPU oracle.
+  sweep     config 2 (B x kv_len) and config 5 (split count) points, cold L2,
+            beside the reference's own Triton kernels timed on the same GPU
+            (``reference_triton``, baseline/time_reference_kernels.py).
+  serving   the Qwen2.5-0.5B-shape model: closed-batch capacity, the Poisson
+            workload of config 4 and the same requests all queued at the start
+            (``saturated``, rate = inf).
 
 ``--impl reference`` times the reference attention math on the host CPU
 (the oracle port: the reference engine ships no CPU kernel of its own and
@@ -80,6 +90,9 @@ def parse_args(argv=None):
     ap.add_argument("--eager", action="store_true",
                     help="launch every timed decode call from Python instead of replaying "
                          "CUDA graphs of them")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip the config-2 / config-5 sweep and the reference Triton timings "
+                         "(run at N=1 only)")
     ap.add_argument("--sweep", action="store_true",
                     help="print one JSON line per decode sweep point (configs 2 and 5) "
                          "instead of the benchmark line")
@@ -152,13 +165,16 @@ def measured_peak_gbs():
 
 
 def ncu_traffic_per_launch(batch: int, kv_len: int):
-    """dram read+write bytes per launch of the decode kernel from the committed
-    ncu summary of this workload, if there is one."""
+    """(dram read+write bytes per launch of the decode kernel, source) from the
+    committed ncu summary of this workload, or (None, reason)."""
     p = REPO / "profiles" / f"decode_split_kernel_b{batch}_l{kv_len}.md"
     if not p.exists():
-        return None
+        return None, "no committed ncu capture of this workload"
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", p.read_text())
-    return int(m.group(1)) if m else None
+    if not m:
+        return None, "no traffic figure in " + str(p.relative_to(REPO))
+    return int(m.group(1)), ("committed ncu capture of the same workload, "
+                             + str(p.relative_to(REPO)) + " (not this run)")
 
 
 class ClockSampler:
@@ -357,9 +373,16 @@ def bf16_peak_tflops(sustained: bool = False):
     return (1400.0 if sustained else 1590.0), "fallback"
 
 
-def mixed_lines(dev, iters: int = 30):
+def mixed_lines(dev, iters: int = 30, cpu: bool = True, e2e_steps: int = 50):
     """Mixed attention: the 512-token-chunk variant (tensor roofline) and
-    config 3 (32 sequences, chunk 1 w.p. 0.5 else U[16,512], budget 2048)."""
+    config 3 (32 sequences, chunk 1 w.p. 0.5 else U[16,512], budget 2048).
+
+    Per case: device time per call (L2 flushed before each call), ``e2e``
+    through the C ABI with the step's own inputs from pinned host memory (q,
+    cu_seqlens, kv_lens, slot ids in; o out; the K/V pool and block table stay
+    resident in HBM, as the engine's KV cache does) and ``cpu_baseline``: the
+    fp32 CPU oracle of the same call on the host's cores."""
+    from custom_inference_engine_b200 import cabi
     from custom_inference_engine_b200 import workloads as W
     from custom_inference_engine_b200.attn import core
     out = {}
@@ -373,6 +396,7 @@ def mixed_lines(dev, iters: int = 30):
                                            generate_on_device=True),
     }
     peak, src = bf16_peak_tflops()
+    stream = torch.cuda.current_stream()
     for name, c in cases.items():
         def fn(c=c):
             core.gqa_mixed_attention_op(c.q, c.k, c.v, max_seqlen=c.max_seqlen,
@@ -383,12 +407,70 @@ def mixed_lines(dev, iters: int = 30):
         ms = statistics.median(time_launches(fn, iters, flush=True, dev=dev))
         flops = c.causal_flops()
         tflops = flops / (ms / 1e3) / 1e12
-        out[name] = {"ms_per_call": ms, "tflops": tflops, "causal_flops": flops,
-                     "tensor_frac": tflops / peak, "peak_tflops": peak, "peak_source": src,
-                     "hbm_gbs": c.algorithmic_bytes() / (ms / 1e3) / 1e9,
-                     "chunks": c.chunk_lens(), "kv_lens": c.kv_lens.tolist(),
-                     "l2": "flushed (256 MB read) before each call"}
+        rec = {"ms_per_call": ms, "tflops": tflops, "causal_flops": flops,
+               "tensor_frac": tflops / peak, "peak_tflops": peak, "peak_source": src,
+               "hbm_gbs": c.algorithmic_bytes() / (ms / 1e3) / 1e9,
+               "chunks": c.chunk_lens(), "kv_lens": c.kv_lens.tolist(),
+               "l2": "flushed (256 MB read) before each call"}
+
+        # e2e: the step's inputs from pinned host memory, o back to the host
+        host = {n: getattr(c, n).cpu().pin_memory()
+                for n in ("q", "cu_seqlens", "kv_lens", "slot_ids")}
+        dbuf = {n: torch.empty_like(getattr(c, n)) for n in host}
+        o_dev = torch.empty_like(c.q)
+        o_host = torch.empty(c.q.shape, dtype=c.q.dtype).pin_memory()
+        B, T = c.slot_ids.shape[0], c.q.shape[1]
+        ws = torch.empty(cabi.mixed_workspace_bytes(B, T, H_KV, 0, dev.index) // 4 + 1,
+                         dtype=torch.float32, device=dev)
+
+        def e2e_step(c=c):
+            for n in host:
+                dbuf[n].copy_(host[n], non_blocking=True)
+            cabi.mixed_attention(dbuf["q"], c.k, c.v, c.max_seqlen, dbuf["cu_seqlens"],
+                                 dbuf["kv_lens"], dbuf["slot_ids"], c.block_table, out=o_dev,
+                                 workspace=ws)
+            o_host.copy_(o_dev, non_blocking=True)
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        rec["e2e"] = {"value": flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                      "ms_per_step": e2e_ms, "steps": e2e_steps,
+                      "h2d_bytes_per_step": sum(t.numel() * t.element_size()
+                                                for t in host.values()),
+                      "d2h_bytes_per_step": o_host.numel() * o_host.element_size(),
+                      "path": "cie_mixed_attention via ctypes; q, cu_seqlens, kv_lens and slot "
+                              "ids copied in from pinned host memory and o read back every "
+                              "step; K/V pool and block table resident in HBM"}
+        if cpu:
+            rec["cpu_baseline"] = mixed_cpu_rate(c)
+        out[name] = rec
     return out
+
+
+def mixed_cpu_rate(c, seconds: float = 6.0):
+    """The fp32 CPU oracle on the same mixed call (all host cores): TFLOP/s."""
+    import oracle
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    args = [t.cpu() for t in (c.q, c.k, c.v)]
+    meta = [t.cpu() for t in (c.cu_seqlens, c.kv_lens, c.slot_ids, c.block_table)]
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        oracle.mixed_attention_fp32(args[0], args[1], args[2], c.max_seqlen, *meta)
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": c.causal_flops() / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+            "kind": "port", "sample": f"{n} call(s) of the whole case, {dt * 1e3:.0f} ms each"}
 
 
 def graph_time_cold(fn, dev, n: int = 20, reps: int = 5) -> float:
@@ -433,15 +515,20 @@ def graph_time_cold(fn, dev, n: int = 20, reps: int = 5) -> float:
     return max(timed(g1) - timed(g0), 0.0) / n
 
 
-def run_sweep(args, dev):
-    """Config 2 (B x kv_len) and config 5 (64 x 32768 split sweep, 8 per GPU) points,
-    each timed on the device with a cold L2 (``graph_time_cold``)."""
+SWEEP_POINTS = ([(b, l, 0) for l in (512, 4096, 16384)
+                 for b in (1, 2, 4, 8, 16, 32, 64, 128, 256)]
+                + [(8, 32768, s) for s in (4, 8, 16, 32, 64)])
+
+
+def sweep_points(dev, points=SWEEP_POINTS):
+    """Config 2 (B x kv_len, default split count) and config 5 (8 x 32768 per
+    GPU, split count swept) points, each timed on the device with a cold L2
+    (``graph_time_cold``); one dict per point."""
     from custom_inference_engine_b200 import cabi
     from custom_inference_engine_b200 import workloads as W
     from custom_inference_engine_b200.attn import core
     peak, _ = measured_peak_gbs()
-    points = [(b, l, 0) for l in (512, 4096, 16384) for b in (1, 2, 4, 8, 16, 32, 64, 128, 256)]
-    points += [(8, 32768, s) for s in (4, 8, 16, 32, 64)]
+    out = []
     for B, L, S in points:
         c = W.make_decode_case([L] * B, seed=5, device=dev, generate_on_device=True)
         splits = S if S > 0 else cabi.decode_default_splits(B, dev.index)
@@ -454,11 +541,53 @@ def run_sweep(args, dev):
         ms = graph_time_cold(fn, dev)
         nbytes = decode_bytes(B, L)
         gbs = nbytes / (ms / 1e3) / 1e9
-        print(json.dumps({"sweep": "config5" if S else "config2", "batch": B, "kv_len": L,
-                          "num_splits": splits, "us_per_call": ms * 1e3, "gbs": gbs,
-                          "frac_of_measured_hbm": gbs / peak}), flush=True)
+        out.append({"sweep": "config5" if S else "config2", "batch": B, "kv_len": L,
+                    "num_splits": splits, "us_per_call": ms * 1e3, "gbs": gbs,
+                    "frac_of_measured_hbm": gbs / peak})
         del c
         torch.cuda.empty_cache()
+    return out
+
+
+def reference_triton_times(points: str = "sweep"):
+    """The reference's own Triton kernels timed on this GPU by
+    baseline/time_reference_kernels.py (a child process: the reference registers
+    the same op names), or the reason they could not be."""
+    script = REPO / "baseline" / "time_reference_kernels.py"
+    if not (REPO / "baseline" / "_ref" / "attn" / "core.py").exists():
+        return {"unavailable": "no copy of the reference in baseline/_ref "
+                               "(baseline/install_reference.py)"}
+    try:
+        run = subprocess.run([sys.executable, str(script), "--points", points],
+                             capture_output=True, text=True, timeout=900)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "timed out after 900 s"}
+    if run.returncode != 0:
+        return {"unavailable": (run.stderr.strip().splitlines() or ["exit %d" % run.returncode])[-1]}
+    return json.loads(run.stdout.strip().splitlines()[-1])
+
+
+def sweep_with_reference(dev):
+    """Our sweep points side by side with the reference Triton kernels' times
+    for the points both measure (same workloads, same timing method)."""
+    ours = sweep_points(dev)
+    ref = reference_triton_times("sweep")
+    by_point = {}
+    for r in ref.get("decode", []):
+        by_point[(r["batch"], r["kv_len"], r["num_programs"])] = r
+    for p in ours:
+        key = (p["batch"], p["kv_len"], p["num_splits"] if p["sweep"] == "config5" else 16)
+        r = by_point.get(key)
+        if r is not None:
+            p["reference_triton_us"] = r["us_per_call"]
+            p["speedup_vs_reference_triton"] = r["us_per_call"] / p["us_per_call"]
+    return ours, ref
+
+
+def run_sweep(args, dev):
+    """--sweep: one JSON line per decode sweep point (configs 2 and 5)."""
+    for p in sweep_points(dev):
+        print(json.dumps(p), flush=True)
 
 
 def serving_line(args, rank, world, dev):
@@ -532,22 +661,26 @@ def serving_line(args, rank, world, dev):
     del graph, runner
     torch.cuda.empty_cache()
     if not args.no_poisson:
-        out["poisson"] = poisson_line(args, model, rank, world, dev)
+        out["poisson"] = poisson_line(args, model, rank, world, dev, args.poisson_rate)
+        # rate = infinity: every request is there at the start (the reference
+        # benchmark's headline mode, README.md:217-227): the engine's capacity
+        out["saturated"] = poisson_line(args, model, rank, world, dev, float("inf"))
     del model
     torch.cuda.empty_cache()
     return out
 
 
-def poisson_line(args, model, rank, world, dev):
-    """Config 4 as specified: one Poisson stream of ``poisson_rate`` x N
-    requests/s (seed 2000) of prompts with lognormal lengths (median 512, sigma
-    0.5, capped at 4096) and outputs of U[64, 512] tokens, sharded round-robin
-    by index over the N GPUs (each GPU sees about ``poisson_rate`` requests/s
-    over the same time window), served per GPU through the continuous-batching
-    loop (serving.py): 33 slots, a 1024-token budget per step, a 32768-token KV
-    pool per GPU. Metrics as the reference's benchmark (5 % trim per GPU; host
-    wall clock, since they are request timestamps): tok/s = new tokens of all
-    GPUs / (latest end - earliest planned arrival over the GPUs)."""
+def poisson_line(args, model, rank, world, dev, rate):
+    """Config 4 as specified: one Poisson stream of ``rate`` x N requests/s
+    (seed 2000; ``rate`` = inf: all requests at the start) of prompts with
+    lognormal lengths (median 512, sigma 0.5, capped at 4096) and outputs of
+    U[64, 512] tokens, sharded round-robin by index over the N GPUs (each GPU
+    sees about ``rate`` requests/s over the same time window), served per GPU
+    through the continuous-batching loop (serving.py): 33 slots, a 1024-token
+    budget per step, a 32768-token KV pool per GPU. Metrics as the reference's
+    benchmark (5 % trim per GPU; host wall clock, since they are request
+    timestamps): tok/s = new tokens of all GPUs / (latest end - earliest
+    planned arrival over the GPUs)."""
     from custom_inference_engine_b200 import model_runner as MR
     from custom_inference_engine_b200 import serving as SV
 
@@ -555,7 +688,7 @@ def poisson_line(args, model, rank, world, dev):
     runner = MR.PagedRunner(model, max_cache_len=pool_tokens, n_slots=n_slots,
                             token_budget=budget)
     engine = SV.RunnerEngine(runner, n_slots)
-    stream = SV.poisson_requests(args.poisson_requests * world, args.poisson_rate * world,
+    stream = SV.poisson_requests(args.poisson_requests * world, rate * world,
                                  seed=2000, vocab=model.config.vocab_size)
     reqs = stream[rank::world]
     torch.cuda.synchronize()
@@ -570,9 +703,12 @@ def poisson_line(args, model, rank, world, dev):
         "tok_s": tokens / duration, "tok_s_rank0": m["tok_s"], "req_s_rank0": m["req_s"],
         "duration_s": duration, "new_tokens": int(tokens), "n_measured_rank0": m["n_measured"],
         "ttft_ms_rank0": m["ttft_ms"], "tpot_ms_rank0": m["tpot_ms"], "steps_rank0": steps,
-        "offered_tok_s": args.poisson_rate * world * 288.0,
-        "workload": f"Poisson {args.poisson_rate:g} req/s per GPU ({args.poisson_rate * world:g} "
-                    f"req/s sharded round-robin over {world} GPU(s)), {args.poisson_requests} "
+        "tok_s_per_gpu": tokens / duration / world,
+        "offered_tok_s": None if math.isinf(rate) else rate * world * 288.0,
+        "workload": (f"Poisson {rate:g} req/s per GPU ({rate * world:g} req/s sharded "
+                     f"round-robin over {world} GPU(s))" if not math.isinf(rate) else
+                     "rate = inf (every request queued at the start)") +
+                    f", {args.poisson_requests} "
                     f"requests per GPU, prompts lognormal (median 512, sigma 0.5, cap 4096), "
                     f"outputs U[64,512], {n_slots} slots, budget {budget}, KV {pool_tokens} "
                     f"tokens per GPU; 5% trim; host wall clock",
@@ -668,11 +804,12 @@ def resident_pool_e2e(args, rank, world, dev, host, dbuf, out_dev, out_host, S, 
         "value": nbytes * world * steps / (ms / 1e3) / 1e9, "unit": UNIT,
         "h2d_bytes_per_step": h_stage.numel(),
         "d2h_bytes_per_step": out_host.numel() * out_host.element_size(), "steps": steps,
-        "path": ("KV pool and block table resident in HBM (the engine's KV cache); per step "
-                 "q, the new K/V rows, lengths and slot ids in one copy from pinned host "
-                 "memory, cie_kv_decode_update + cie_decode_attention via ctypes, o read "
-                 "back; copies of neighbouring steps overlap the step's kernels (two "
-                 "buffers, copy streams)"),
+        "path": ("decode step through the C ABI as the engine runs it: KV pool and block "
+                 "table resident in HBM (the engine's KV cache, copied in once); per step "
+                 "the step's inputs -- q, the new K/V rows, lengths and slot ids -- in one "
+                 "copy from pinned host memory, cie_kv_decode_update + cie_decode_attention "
+                 "via ctypes, o read back; copies of neighbouring steps overlap the step's "
+                 "kernels (two buffers, copy streams)"),
         "device_error_bits": native.device_errors(dev.index, clear=True),
     }
 
@@ -739,6 +876,7 @@ def run_ours(args, rank, world, local):
     kernel_ms = local_ms / args.steps  # every step is one decode call on this stream
     achieved = nbytes / (kernel_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak_gbs()
+    traffic, traffic_src = ncu_traffic_per_launch(B, L)
     errs = native.device_errors(dev.index, clear=True)
 
     # ---- e2e: C ABI with host buffers ---------------------------------------
@@ -786,21 +924,26 @@ def run_ours(args, rank, world, local):
             "steps": args.steps, "warmup": max(args.warmup, 3),
             "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16 in / fp32 accumulate", "data": "synthetic",
-            "config": dict(workload_config(args, world), num_splits=S,
-                           timing=("eager: one Python launch per call" if args.eager else
-                                   f"CUDA graphs of {chunk} consecutive decode calls, replayed "
-                                   f"(the engine's decode steps are CUDA graphs)")),
+            "config": workload_config(args, world),
+            "value_per_gpu": value / world,
+            "num_splits": S,
+            "timing": ("eager: one Python launch per call" if args.eager else
+                       f"CUDA graphs of {chunk} consecutive decode calls, replayed "
+                       f"(the engine's decode steps are CUDA graphs)"),
             "pct_of_peak": 100.0 * achieved / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                         "traffic": ncu_traffic_per_launch(B, L),
+                         "traffic": traffic, "traffic_source": traffic_src,
                          "algorithmic_bytes_per_launch": nbytes,
                          "kernel": "decode_split_kernel<2>" + (" + decode_merge_kernel"
                                                                if S > 1 else "")},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "path": "cie_decode_attention via ctypes, pinned host buffers",
-                    "output_matches_device_leg": bool(ok), "resident_pool": resident},
+            "e2e": dict(resident, full_pool_copy={
+                "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "path": "cie_decode_attention via ctypes; every step copies q, both K/V "
+                        "pools, lens, slot ids and the block table from pinned host memory "
+                        "and reads o back (PCIe-bound: the whole pool crosses every step)",
+                "output_matches_device_leg": bool(ok)}),
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks.summary(),
             "device_error_bits": errs,
@@ -808,7 +951,10 @@ def run_ours(args, rank, world, local):
         if serving is not None:
             result["serving"] = serving
         if not args.no_mixed:
-            result["mixed"] = mixed_lines(dev)
+            result["mixed"] = mixed_lines(dev, cpu=world == 1 and not args.no_cpu_baseline)
+        if world == 1 and not args.no_sweep:
+            result["sweep"], ref = sweep_with_reference(dev)
+            result["reference_triton"] = ref
         if not args.no_cpu_baseline and world == 1:
             gbs, cores, sample = cpu_oracle_rate(L, args.cpu_seconds)
             result["cpu_baseline"] = {"value": gbs, "unit": UNIT, "cores": cores, "kind": "port",

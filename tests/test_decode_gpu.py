@@ -75,8 +75,12 @@ def test_config1_full(cuda_device):
 
 
 @pytest.mark.parametrize("B,L", [(1, 512), (2, 16384), (8, 4096), (32, 512), (64, 4096),
-                                 (128, 512), (256, 4096)])
+                                 (128, 512), (256, 4096), (256, 16384)])
 def test_config2_points_against_fp32(B, L, cuda_device):
+    # (256, 16384) is the largest config-2 pool: 262 145 pages, 2 GiB per K or
+    # V, K/V offsets up to 5.4e8 elements and 4.2 M block-table entries, the
+    # size where the reference's int32 offset guards (attn/core.py:24-34)
+    # start to matter; this build addresses the pools with 64-bit offsets
     c = W.make_decode_case([L] * B, seed=7, device=cuda_device, generate_on_device=True)
     ref = torch_decode_fp32(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table)
     o = cabi.decode_attention(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table)
