@@ -19,6 +19,15 @@ def _p(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+def _entry(name: str, block_table: torch.Tensor):
+    """Entry point ``name``, or its ``_bt32`` variant for an int32 block table."""
+    if block_table.dtype == torch.int32:
+        name += "_bt32"
+    elif block_table.dtype != torch.int64:
+        raise TypeError(f"block_table must be int64 or int32, not {block_table.dtype}")
+    return getattr(native.lib(), name)
+
+
 def decode_workspace_bytes(batch: int, num_q_heads: int, head_dim: int, num_splits: int) -> int:
     return int(native.lib().cie_decode_workspace_bytes(batch, num_q_heads, head_dim, num_splits))
 
@@ -39,7 +48,7 @@ def decode_attention(q, k, v, lens, slot_ids, block_table, out=None, num_splits:
     if need > 0 and workspace is None:
         workspace = torch.empty(need // 4, dtype=torch.float32, device=q.device)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    st = native.lib().cie_decode_attention(
+    st = _entry("cie_decode_attention", block_table)(
         _p(q), _p(k), _p(v), _p(lens), _p(slot_ids), _p(block_table), _p(out), _p(workspace),
         ws_bytes, B, hq, k.shape[1], d, k.shape[2], k.shape[0], block_table.shape[0],
         block_table.stride(0), k.stride(0), k.stride(1), S, native.stream_ptr(stream))
@@ -79,7 +88,7 @@ def mixed_attention(q, k, v, max_seqlen: int, cu_seqlens, kv_lens, slot_ids, blo
         need = mixed_workspace_bytes(B, T, k.shape[1], num_splits, q.device.index or 0)
         workspace = torch.empty(max(need // 4, 1), dtype=torch.float32, device=q.device)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    st = native.lib().cie_mixed_attention(
+    st = _entry("cie_mixed_attention", block_table)(
         _p(q), _p(k), _p(v), int(max_seqlen), _p(cu_seqlens), _p(kv_lens), _p(slot_ids),
         _p(block_table), _p(out), _p(workspace), ws_bytes, B, T, q.shape[2], k.shape[1],
         q.shape[3], k.shape[2], k.shape[0], block_table.shape[0], block_table.stride(0),
@@ -91,7 +100,7 @@ def mixed_attention(q, k, v, max_seqlen: int, cu_seqlens, kv_lens, slot_ids, blo
 def kv_decode_update(k_cache, v_cache, lens, slot_ids, block_table, k_new, v_new,
                      stream=None) -> None:
     """cie_kv_decode_update; ``lens`` is the per-slot length tensor (n_slots,)."""
-    st = native.lib().cie_kv_decode_update(
+    st = _entry("cie_kv_decode_update", block_table)(
         _p(k_cache), _p(v_cache), _p(lens), _p(slot_ids), _p(block_table), _p(k_new), _p(v_new),
         slot_ids.shape[0], k_cache.shape[1], k_cache.shape[3], k_cache.shape[2],
         k_cache.shape[0], min(lens.shape[0], block_table.shape[0]), block_table.stride(0),
@@ -123,7 +132,7 @@ def rope_kv_decode_update(qkv, cos, sin, k_cache, v_cache, lens, slot_ids, block
     """cie_rope_kv_decode_update: rotated q (returned) and the token's rotated k / v
     written at its slot's current length."""
     out, hq = _rope_q_out(qkv, k_cache, out)
-    st = native.lib().cie_rope_kv_decode_update(
+    st = _entry("cie_rope_kv_decode_update", block_table)(
         _p(qkv), qkv.stride(1), _p(cos), _p(sin), cos.stride(1), _p(out), _p(k_cache),
         _p(v_cache), _p(lens), _p(slot_ids), _p(block_table), slot_ids.shape[0], hq,
         k_cache.shape[1], k_cache.shape[3], k_cache.shape[2], k_cache.shape[0],
@@ -160,7 +169,7 @@ def rope_kv_decode_attention(qkv, cos, sin, k_cache, v_cache, lens, slot_ids, bl
     if need > 0 and workspace is None:
         workspace = torch.empty(need // 4, dtype=torch.float32, device=qkv.device)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    st = native.lib().cie_rope_kv_decode_attention(
+    st = _entry("cie_rope_kv_decode_attention", block_table)(
         _p(qkv), qkv.stride(1), _p(cos), _p(sin), cos.stride(1), _p(k_cache), _p(v_cache),
         _p(lens), _p(slot_ids), _p(block_table), _p(out), _p(workspace), ws_bytes, B, hq,
         k_cache.shape[1], d, k_cache.shape[2], k_cache.shape[0],

@@ -39,6 +39,20 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 
 // ---------------------------------------------------------------------------
+// Block table: row-major (n_slots, stride) page ids, int64 (the reference's
+// layout, kv_cache/storage.py:52-56) or int32 (the *_bt32 entry points). The
+// width is uniform across a launch, so the branch costs nothing.
+// ---------------------------------------------------------------------------
+struct BlockTable {
+  const void* ptr;
+  int wide;  // 1: int64 entries, 0: int32 entries
+  __device__ __forceinline__ int64_t at(int64_t i) const {
+    return wide ? static_cast<const int64_t*>(ptr)[i]
+                : static_cast<int64_t>(static_cast<const int32_t*>(ptr)[i]);
+  }
+};
+
+// ---------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {

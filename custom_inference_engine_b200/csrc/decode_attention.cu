@@ -52,7 +52,7 @@ struct Params {
   const __half* q;            // (B, H_q, D)
   const int64_t* lens;        // (B,)
   const int64_t* slot_ids;    // (B,)
-  const int64_t* block_table; // (n_slots, bt_stride)
+  BlockTable block_table;     // (n_slots, bt_stride)
   __half* o;                  // (B, H_q, D)
   float* ws_acc;              // (B, S, H_q, D)
   float* ws_ml;               // (B, S, H_q, 2)
@@ -202,10 +202,10 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
     }
-    const int64_t* bt_row = p.block_table + slot * p.bt_stride + page_begin;
+    const int64_t bt_row = slot * p.bt_stride + page_begin;
     auto page_id = [&](int j) -> int {  // block-table entry j of this split, checked
       if (j >= n) return 0;
-      int64_t pid = bt_row[j];
+      int64_t pid = p.block_table.at(bt_row + j);
       if (pid < 0 || pid >= p.n_pages) {
         raise_error(CIE_DEVERR_BAD_PAGE);
         pid = 0;
@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(val.x),
                      "r"(val.y), "r"(val.z), "r"(val.w)
                      : "memory");
-        int64_t pg = p.block_table[slot * p.bt_stride + (Li - 1) / kPage];
+        int64_t pg = p.block_table.at(slot * p.bt_stride + (Li - 1) / kPage);
         if (pg >= 0 && pg < p.n_pages) {
           __half* dst = (lane < 8 ? p.k_cache : p.v_cache) + pg * p.page_stride +
                         h * p.head_stride + new_row * kD + c * 8;
@@ -633,7 +633,7 @@ struct FusedRope {
 
 template <int HKV>
 int launch(const void* q, const void* k, const void* v, const int64_t* lens,
-           const int64_t* slot_ids, const int64_t* block_table, void* o, float* ws, int batch,
+           const int64_t* slot_ids, BlockTable block_table, void* o, float* ws, int batch,
            int64_t n_pages, int64_t n_slots, int64_t bt_stride, int64_t page_stride,
            int64_t head_stride, int S, cudaStream_t stream, const FusedRope* rope = nullptr) {
   using C = Cfg<HKV>;
@@ -742,7 +742,7 @@ namespace decode {
 // workspace); q is null exactly when `rope` is given. On success *splits is
 // the split count the call will use (0 when batch == 0: nothing to do).
 int check_args(const void* q, const void* k, const void* v, const int64_t* lens,
-               const int64_t* slot_ids, const int64_t* block_table, const void* o, int batch,
+               const int64_t* slot_ids, const void* block_table, const void* o, int batch,
                int num_q_heads, int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
                int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
                int64_t kv_head_stride, int num_splits, const FusedRope* rope, int* splits) {
@@ -787,13 +787,13 @@ int check_args(const void* q, const void* k, const void* v, const int64_t* lens,
 
 // Argument checks and dispatch of the decode entry points.
 int entry(const void* q, const void* k, const void* v, const int64_t* lens,
-          const int64_t* slot_ids, const int64_t* block_table, void* o, void* workspace,
+          const int64_t* slot_ids, BlockTable block_table, void* o, void* workspace,
           size_t workspace_bytes, int batch, int num_q_heads, int num_kv_heads, int head_dim,
           int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
           int64_t kv_page_stride, int64_t kv_head_stride, int num_splits, cie_stream_t stream,
           const FusedRope* rope) {
   int S = 0;
-  const int st = check_args(q, k, v, lens, slot_ids, block_table, o, batch, num_q_heads,
+  const int st = check_args(q, k, v, lens, slot_ids, block_table.ptr, o, batch, num_q_heads,
                             num_kv_heads, head_dim, page_size, n_pages, n_slots, bt_stride,
                             kv_page_stride, kv_head_stride, num_splits, rope, &S);
   if (st != CIE_OK || S == 0) return st;
@@ -831,10 +831,38 @@ int cie_decode_attention(const void* q, const void* k, const void* v, const int6
                          int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
                          int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
                          int64_t kv_head_stride, int num_splits, cie_stream_t stream) {
-  return cie::decode::entry(q, k, v, lens, slot_ids, block_table, o, workspace, workspace_bytes,
-                            batch, num_q_heads, num_kv_heads, head_dim, page_size, n_pages,
-                            n_slots, bt_stride, kv_page_stride, kv_head_stride, num_splits, stream,
-                            nullptr);
+  return cie::decode::entry(q, k, v, lens, slot_ids, cie::BlockTable{block_table, 1}, o,
+                            workspace, workspace_bytes, batch, num_q_heads, num_kv_heads,
+                            head_dim, page_size, n_pages, n_slots, bt_stride, kv_page_stride,
+                            kv_head_stride, num_splits, stream, nullptr);
+}
+
+int cie_decode_attention_bt32(const void* q, const void* k, const void* v, const int64_t* lens,
+                              const int64_t* slot_ids, const int32_t* block_table, void* o,
+                              void* workspace, size_t workspace_bytes, int batch, int num_q_heads,
+                              int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
+                              int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
+                              int64_t kv_head_stride, int num_splits, cie_stream_t stream) {
+  return cie::decode::entry(q, k, v, lens, slot_ids, cie::BlockTable{block_table, 0}, o,
+                            workspace, workspace_bytes, batch, num_q_heads, num_kv_heads,
+                            head_dim, page_size, n_pages, n_slots, bt_stride, kv_page_stride,
+                            kv_head_stride, num_splits, stream, nullptr);
+}
+
+static int rope_kv_decode_attention(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                                    const void* sin, int64_t cs_tok_stride, void* k_cache,
+                                    void* v_cache, const int64_t* lens, const int64_t* slot_ids,
+                                    cie::BlockTable block_table, void* o, void* workspace,
+                                    size_t workspace_bytes, int batch, int num_q_heads,
+                                    int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
+                                    int64_t n_slots, int64_t bt_stride, int64_t cache_page_stride,
+                                    int64_t cache_head_stride, int num_splits,
+                                    cie_stream_t stream) {
+  const cie::decode::FusedRope rope{qkv, qkv_tok_stride, cos, sin, cs_tok_stride};
+  return cie::decode::entry(nullptr, k_cache, v_cache, lens, slot_ids, block_table, o, workspace,
+                            workspace_bytes, batch, num_q_heads, num_kv_heads, head_dim,
+                            page_size, n_pages, n_slots, bt_stride, cache_page_stride,
+                            cache_head_stride, num_splits, stream, &rope);
 }
 
 int cie_rope_kv_decode_attention(const void* qkv, int64_t qkv_tok_stride, const void* cos,
@@ -845,11 +873,25 @@ int cie_rope_kv_decode_attention(const void* qkv, int64_t qkv_tok_stride, const 
                                  int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
                                  int64_t n_slots, int64_t bt_stride, int64_t cache_page_stride,
                                  int64_t cache_head_stride, int num_splits, cie_stream_t stream) {
-  const cie::decode::FusedRope rope{qkv, qkv_tok_stride, cos, sin, cs_tok_stride};
-  return cie::decode::entry(nullptr, k_cache, v_cache, lens, slot_ids, block_table, o, workspace,
-                            workspace_bytes, batch, num_q_heads, num_kv_heads, head_dim,
-                            page_size, n_pages, n_slots, bt_stride, cache_page_stride,
-                            cache_head_stride, num_splits, stream, &rope);
+  return rope_kv_decode_attention(qkv, qkv_tok_stride, cos, sin, cs_tok_stride, k_cache, v_cache,
+                                  lens, slot_ids, cie::BlockTable{block_table, 1}, o, workspace,
+                                  workspace_bytes, batch, num_q_heads, num_kv_heads, head_dim,
+                                  page_size, n_pages, n_slots, bt_stride, cache_page_stride,
+                                  cache_head_stride, num_splits, stream);
+}
+
+int cie_rope_kv_decode_attention_bt32(
+    const void* qkv, int64_t qkv_tok_stride, const void* cos, const void* sin,
+    int64_t cs_tok_stride, void* k_cache, void* v_cache, const int64_t* lens,
+    const int64_t* slot_ids, const int32_t* block_table, void* o, void* workspace,
+    size_t workspace_bytes, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+    int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride, int64_t cache_page_stride,
+    int64_t cache_head_stride, int num_splits, cie_stream_t stream) {
+  return rope_kv_decode_attention(qkv, qkv_tok_stride, cos, sin, cs_tok_stride, k_cache, v_cache,
+                                  lens, slot_ids, cie::BlockTable{block_table, 0}, o, workspace,
+                                  workspace_bytes, batch, num_q_heads, num_kv_heads, head_dim,
+                                  page_size, n_pages, n_slots, bt_stride, cache_page_stride,
+                                  cache_head_stride, num_splits, stream);
 }
 
 }  // extern "C"

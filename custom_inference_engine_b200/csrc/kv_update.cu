@@ -35,7 +35,7 @@ template <bool kVec>
 __global__ void decode_update_kernel(__half* __restrict__ k_cache, __half* __restrict__ v_cache,
                                      const int64_t* __restrict__ lens,
                                      const int64_t* __restrict__ slot_ids,
-                                     const int64_t* __restrict__ block_table, Src src, int batch,
+                                     BlockTable block_table, Src src, int batch,
                                      int hkv, int head_dim, int page_size, int64_t n_pages,
                                      int64_t n_slots, int64_t bt_stride, int64_t page_stride,
                                      int64_t head_stride) {
@@ -57,7 +57,7 @@ __global__ void decode_update_kernel(__half* __restrict__ k_cache, __half* __res
     raise_error(CIE_DEVERR_BAD_LENGTH);
     return;
   }
-  const int64_t page = block_table[slot * bt_stride + pos / page_size];
+  const int64_t page = block_table.at(slot * bt_stride + pos / page_size);
   if (page < 0 || page >= n_pages) {
     raise_error(CIE_DEVERR_BAD_PAGE);
     return;
@@ -127,13 +127,14 @@ bool vec_ok(const void* k_cache, const void* v_cache, const Src& s, int64_t page
 
 extern "C" {
 
-int cie_kv_decode_update(void* k_cache, void* v_cache, const int64_t* lens,
-                         const int64_t* slot_ids, const int64_t* block_table, const void* k_new,
-                         const void* v_new, int batch, int num_kv_heads, int head_dim,
-                         int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
-                         int64_t cache_page_stride, int64_t cache_head_stride,
-                         int64_t k_tok_stride, int64_t k_head_stride, int64_t v_tok_stride,
-                         int64_t v_head_stride, cie_stream_t stream) {
+static int kv_decode_update(void* k_cache, void* v_cache, const int64_t* lens,
+                            const int64_t* slot_ids, cie::BlockTable block_table,
+                            const void* k_new, const void* v_new, int batch, int num_kv_heads,
+                            int head_dim, int page_size, int64_t n_pages, int64_t n_slots,
+                            int64_t bt_stride, int64_t cache_page_stride,
+                            int64_t cache_head_stride, int64_t k_tok_stride,
+                            int64_t k_head_stride, int64_t v_tok_stride, int64_t v_head_stride,
+                            cie_stream_t stream) {
   using namespace cie;
   using namespace cie::kvupd;
   if (batch < 0) return fail(CIE_ERR_INVALID_ARGUMENT, "batch < 0");
@@ -141,7 +142,7 @@ int cie_kv_decode_update(void* k_cache, void* v_cache, const int64_t* lens,
   int st = check_common(k_cache, v_cache, k_new, v_new, num_kv_heads, head_dim, page_size, n_pages,
                         cache_page_stride, cache_head_stride);
   if (st != CIE_OK) return st;
-  if (!lens || !slot_ids || !block_table)
+  if (!lens || !slot_ids || !block_table.ptr)
     return fail(CIE_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (n_slots < 1 || bt_stride < 1) return fail(CIE_ERR_INVALID_ARGUMENT, "n_slots / bt_stride");
   Src src{static_cast<const __half*>(k_new), static_cast<const __half*>(v_new), k_tok_stride,
@@ -164,6 +165,33 @@ int cie_kv_decode_update(void* k_cache, void* v_cache, const int64_t* lens,
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "decode_update launch: %s", cudaGetErrorString(e));
   return CIE_OK;
+}
+
+int cie_kv_decode_update(void* k_cache, void* v_cache, const int64_t* lens,
+                         const int64_t* slot_ids, const int64_t* block_table, const void* k_new,
+                         const void* v_new, int batch, int num_kv_heads, int head_dim,
+                         int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                         int64_t cache_page_stride, int64_t cache_head_stride,
+                         int64_t k_tok_stride, int64_t k_head_stride, int64_t v_tok_stride,
+                         int64_t v_head_stride, cie_stream_t stream) {
+  return kv_decode_update(k_cache, v_cache, lens, slot_ids, cie::BlockTable{block_table, 1},
+                          k_new, v_new, batch, num_kv_heads, head_dim, page_size, n_pages,
+                          n_slots, bt_stride, cache_page_stride, cache_head_stride, k_tok_stride,
+                          k_head_stride, v_tok_stride, v_head_stride, stream);
+}
+
+int cie_kv_decode_update_bt32(void* k_cache, void* v_cache, const int64_t* lens,
+                              const int64_t* slot_ids, const int32_t* block_table,
+                              const void* k_new, const void* v_new, int batch, int num_kv_heads,
+                              int head_dim, int page_size, int64_t n_pages, int64_t n_slots,
+                              int64_t bt_stride, int64_t cache_page_stride,
+                              int64_t cache_head_stride, int64_t k_tok_stride,
+                              int64_t k_head_stride, int64_t v_tok_stride,
+                              int64_t v_head_stride, cie_stream_t stream) {
+  return kv_decode_update(k_cache, v_cache, lens, slot_ids, cie::BlockTable{block_table, 0},
+                          k_new, v_new, batch, num_kv_heads, head_dim, page_size, n_pages,
+                          n_slots, bt_stride, cache_page_stride, cache_head_stride, k_tok_stride,
+                          k_head_stride, v_tok_stride, v_head_stride, stream);
 }
 
 int cie_kv_mixed_update(void* k_cache, void* v_cache, const int64_t* pages,

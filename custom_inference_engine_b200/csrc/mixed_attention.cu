@@ -130,7 +130,7 @@ struct Params {
   const int64_t* cu_seqlens;
   const int64_t* kv_lens;
   const int64_t* slot_ids;
-  const int64_t* block_table;
+  BlockTable block_table;
   __half* o;
   Plan plan;
   int64_t total_tokens;
@@ -599,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_4d(sQ + kQBytes, &tm_q, bars.q_full(), 0, 0, h,
                       static_cast<int>(start) + pi.tok0 + kTileTokens);
       }
-      const int64_t* bt_row = p.block_table + slot * p.bt_stride;
+      const int64_t bt_row = slot * p.bt_stride;
       for (int j = 0; j < n_blocks; ++j) {
         const int s = j % kStages;
         const uint32_t use = static_cast<uint32_t>(j / kStages);
@@ -607,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane < kPagesPerBlock) {
           const int lp = (blk0 + j) * kPagesPerBlock + lane;
           if (lp < n_valid_pages) {
-            int64_t pid = bt_row[lp];
+            int64_t pid = p.block_table.at(bt_row + lp);
             if (pid < 0 || pid >= p.n_pages) {
               raise_error(CIE_DEVERR_BAD_PAGE);
               pid = 0;
@@ -966,20 +966,23 @@ size_t cie_mixed_workspace_bytes(int batch, int64_t total_tokens, int num_kv_hea
   return plan_sizes(batch, total_tokens, num_kv_heads, num_splits, device_sms(device)).bytes;
 }
 
-int cie_mixed_attention(const void* q, const void* k, const void* v, int64_t max_seqlen,
-                        const int64_t* cu_seqlens, const int64_t* kv_lens,
-                        const int64_t* slot_ids, const int64_t* block_table, void* o,
-                        void* workspace, size_t workspace_bytes, int batch,
-                        int64_t total_tokens, int num_q_heads, int num_kv_heads, int head_dim,
-                        int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
-                        int64_t kv_page_stride, int64_t kv_head_stride, int num_splits,
-                        cie_stream_t stream) {
-  using namespace cie;
-  using namespace cie::mixed;
+}  // extern "C"
+
+namespace cie {
+namespace mixed {
+
+// Argument checks, tensor maps and the two launches of cie_mixed_attention
+// (and of its int32-block-table variant).
+int entry(const void* q, const void* k, const void* v, int64_t max_seqlen,
+          const int64_t* cu_seqlens, const int64_t* kv_lens, const int64_t* slot_ids,
+          BlockTable block_table, void* o, void* workspace, size_t workspace_bytes, int batch,
+          int64_t total_tokens, int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+          int64_t n_pages, int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
+          int64_t kv_head_stride, int num_splits, cie_stream_t stream) {
   if (batch < 0 || total_tokens < 0 || max_seqlen < 0)
     return fail(CIE_ERR_INVALID_ARGUMENT, "negative batch / total_tokens / max_seqlen");
   if (batch == 0 || total_tokens == 0 || max_seqlen == 0) return CIE_OK;
-  if (!q || !k || !v || !cu_seqlens || !kv_lens || !slot_ids || !block_table || !o)
+  if (!q || !k || !v || !cu_seqlens || !kv_lens || !slot_ids || !block_table.ptr || !o)
     return fail(CIE_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (head_dim != kD || page_size != kPage)
     return fail(CIE_ERR_UNSUPPORTED, "head_dim %d / page_size %d (supported: 64 / 16)", head_dim,
@@ -1087,6 +1090,39 @@ int cie_mixed_attention(const void* q, const void* k, const void* v, int64_t max
   e = cudaLaunchKernelEx(&cfg, mixed_attention_kernel, tm_q, tm_k, tm_v, p);
   if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "mixed launch: %s", cudaGetErrorString(e));
   return CIE_OK;
+}
+
+}  // namespace mixed
+}  // namespace cie
+
+extern "C" {
+
+int cie_mixed_attention(const void* q, const void* k, const void* v, int64_t max_seqlen,
+                        const int64_t* cu_seqlens, const int64_t* kv_lens,
+                        const int64_t* slot_ids, const int64_t* block_table, void* o,
+                        void* workspace, size_t workspace_bytes, int batch,
+                        int64_t total_tokens, int num_q_heads, int num_kv_heads, int head_dim,
+                        int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                        int64_t kv_page_stride, int64_t kv_head_stride, int num_splits,
+                        cie_stream_t stream) {
+  return cie::mixed::entry(q, k, v, max_seqlen, cu_seqlens, kv_lens, slot_ids,
+                           cie::BlockTable{block_table, 1}, o, workspace, workspace_bytes, batch,
+                           total_tokens, num_q_heads, num_kv_heads, head_dim, page_size, n_pages,
+                           n_slots, bt_stride, kv_page_stride, kv_head_stride, num_splits, stream);
+}
+
+int cie_mixed_attention_bt32(const void* q, const void* k, const void* v, int64_t max_seqlen,
+                             const int64_t* cu_seqlens, const int64_t* kv_lens,
+                             const int64_t* slot_ids, const int32_t* block_table, void* o,
+                             void* workspace, size_t workspace_bytes, int batch,
+                             int64_t total_tokens, int num_q_heads, int num_kv_heads,
+                             int head_dim, int page_size, int64_t n_pages, int64_t n_slots,
+                             int64_t bt_stride, int64_t kv_page_stride, int64_t kv_head_stride,
+                             int num_splits, cie_stream_t stream) {
+  return cie::mixed::entry(q, k, v, max_seqlen, cu_seqlens, kv_lens, slot_ids,
+                           cie::BlockTable{block_table, 0}, o, workspace, workspace_bytes, batch,
+                           total_tokens, num_q_heads, num_kv_heads, head_dim, page_size, n_pages,
+                           n_slots, bt_stride, kv_page_stride, kv_head_stride, num_splits, stream);
 }
 
 }  // extern "C"

@@ -34,7 +34,7 @@ struct Args {
   // decode addressing (pages == nullptr) or mixed addressing
   const int64_t* lens;
   const int64_t* slot_ids;
-  const int64_t* block_table;
+  BlockTable block_table;
   const int64_t* pages;
   const int64_t* offsets;
   int64_t num_tokens;
@@ -99,7 +99,7 @@ __global__ void rope_kv_kernel(const Args a) {
         if (row == a.hq && c == 0) raise_error(CIE_DEVERR_BAD_LENGTH);
         return;
       }
-      page = a.block_table[slot * a.bt_stride + pos / a.page_size];
+      page = a.block_table.at(slot * a.bt_stride + pos / a.page_size);
       off = pos % a.page_size;
     } else {
       page = a.pages[t];
@@ -163,16 +163,16 @@ int launch(Args a, int head_dim, cie_stream_t stream) {
 
 extern "C" {
 
-int cie_rope_kv_decode_update(const void* qkv, int64_t qkv_tok_stride, const void* cos,
-                              const void* sin, int64_t cs_tok_stride, void* q_out,
-                              void* k_cache, void* v_cache, const int64_t* lens,
-                              const int64_t* slot_ids, const int64_t* block_table, int batch,
-                              int num_q_heads, int num_kv_heads, int head_dim, int page_size,
-                              int64_t n_pages, int64_t n_slots, int64_t bt_stride,
-                              int64_t cache_page_stride, int64_t cache_head_stride,
-                              cie_stream_t stream) {
+static int rope_kv_decode_update(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                                 const void* sin, int64_t cs_tok_stride, void* q_out,
+                                 void* k_cache, void* v_cache, const int64_t* lens,
+                                 const int64_t* slot_ids, cie::BlockTable block_table, int batch,
+                                 int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                 int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                                 int64_t cache_page_stride, int64_t cache_head_stride,
+                                 cie_stream_t stream) {
   using namespace cie;
-  if (batch > 0 && (!lens || !slot_ids || !block_table))
+  if (batch > 0 && (!lens || !slot_ids || !block_table.ptr))
     return fail(CIE_ERR_INVALID_ARGUMENT, "null lens / slot_ids / block_table");
   if (batch > 0 && (n_slots < 1 || bt_stride < 1))
     return fail(CIE_ERR_INVALID_ARGUMENT, "n_slots / bt_stride must be >= 1");
@@ -198,6 +198,34 @@ int cie_rope_kv_decode_update(const void* qkv, int64_t qkv_tok_stride, const voi
   a.n_slots = n_slots;
   a.bt_stride = bt_stride;
   return rope::launch(a, head_dim, stream);
+}
+
+int cie_rope_kv_decode_update(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                              const void* sin, int64_t cs_tok_stride, void* q_out,
+                              void* k_cache, void* v_cache, const int64_t* lens,
+                              const int64_t* slot_ids, const int64_t* block_table, int batch,
+                              int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                              int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                              int64_t cache_page_stride, int64_t cache_head_stride,
+                              cie_stream_t stream) {
+  return rope_kv_decode_update(qkv, qkv_tok_stride, cos, sin, cs_tok_stride, q_out, k_cache,
+                               v_cache, lens, slot_ids, cie::BlockTable{block_table, 1}, batch,
+                               num_q_heads, num_kv_heads, head_dim, page_size, n_pages, n_slots,
+                               bt_stride, cache_page_stride, cache_head_stride, stream);
+}
+
+int cie_rope_kv_decode_update_bt32(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                                   const void* sin, int64_t cs_tok_stride, void* q_out,
+                                   void* k_cache, void* v_cache, const int64_t* lens,
+                                   const int64_t* slot_ids, const int32_t* block_table, int batch,
+                                   int num_q_heads, int num_kv_heads, int head_dim,
+                                   int page_size, int64_t n_pages, int64_t n_slots,
+                                   int64_t bt_stride, int64_t cache_page_stride,
+                                   int64_t cache_head_stride, cie_stream_t stream) {
+  return rope_kv_decode_update(qkv, qkv_tok_stride, cos, sin, cs_tok_stride, q_out, k_cache,
+                               v_cache, lens, slot_ids, cie::BlockTable{block_table, 0}, batch,
+                               num_q_heads, num_kv_heads, head_dim, page_size, n_pages, n_slots,
+                               bt_stride, cache_page_stride, cache_head_stride, stream);
 }
 
 int cie_rope_kv_mixed_update(const void* qkv, int64_t qkv_tok_stride, const void* cos,

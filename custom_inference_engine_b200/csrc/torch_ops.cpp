@@ -29,6 +29,21 @@ void check_i64(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
 }
 
+// The block table holds int64 page ids (the reference's layout) or int32 ones
+// (the *_bt32 entry points); the ops take either.
+void check_table(const at::Tensor& t) {
+  TORCH_CHECK(t.scalar_type() == at::kLong || t.scalar_type() == at::kInt,
+              "block_table must be int64 or int32");
+  TORCH_CHECK(t.is_cuda(), "block_table must be a CUDA tensor");
+}
+
+// Calls `call(fn64, int64 table)` or `call(fn32, int32 table)` by the table's dtype.
+template <typename Call, typename F64, typename F32>
+int with_table(const at::Tensor& t, Call&& call, F64 fn64, F32 fn32) {
+  return t.scalar_type() == at::kInt ? call(fn32, t.data_ptr<int32_t>())
+                                     : call(fn64, t.data_ptr<int64_t>());
+}
+
 void check_kv_pool(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v) {
   TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(), "q, k, v must be CUDA tensors");
   TORCH_CHECK(q.scalar_type() == at::kHalf && k.scalar_type() == at::kHalf &&
@@ -50,7 +65,7 @@ at::Tensor decode_impl(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   check_kv_pool(q, k, v);
   check_i64(lens, "lens");
   check_i64(slot_ids, "slot_ids");
-  check_i64(block_table, "block_table");
+  check_table(block_table);
   const int64_t B = slot_ids.size(0);
   TORCH_CHECK(lens.dim() == 1 && lens.size(0) == B, "lens must be (B,)");
   TORCH_CHECK(block_table.dim() == 2 && block_table.size(1) == k.size(0),
@@ -70,14 +85,18 @@ at::Tensor decode_impl(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   if (ws_bytes > 0)
     ws = at::empty({static_cast<int64_t>(ws_bytes / sizeof(float))},
                    q.options().dtype(at::kFloat));
-  const int st = cie_decode_attention(
-      q.data_ptr(), k.data_ptr(), v.data_ptr(), lens.data_ptr<int64_t>(),
-      slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(), o.data_ptr(),
-      ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, static_cast<int>(B),
-      static_cast<int>(q.size(2)), static_cast<int>(k.size(1)), static_cast<int>(q.size(3)),
-      static_cast<int>(k.size(2)), k.size(0), block_table.size(0), block_table.stride(0),
-      k.stride(0), k.stride(1), S,
-      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  const int st = with_table(
+      block_table,
+      [&](auto fn, auto* table) {
+        return fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), lens.data_ptr<int64_t>(),
+          slot_ids.data_ptr<int64_t>(), table, o.data_ptr(),
+          ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, static_cast<int>(B),
+          static_cast<int>(q.size(2)), static_cast<int>(k.size(1)), static_cast<int>(q.size(3)),
+          static_cast<int>(k.size(2)), k.size(0), block_table.size(0), block_table.stride(0),
+          k.stride(0), k.stride(1), S,
+          reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+      },
+      cie_decode_attention, cie_decode_attention_bt32);
   check_status(st, "gqa_decode_attention");
   return o;
 }
@@ -105,7 +124,7 @@ at::Tensor gqa_mixed_attention(const at::Tensor& q, const at::Tensor& k, const a
   check_i64(cu_seqlens, "cu_seqlens");
   check_i64(kv_lens, "kv_lens");
   check_i64(slot_ids, "slot_ids");
-  check_i64(block_table, "block_table");
+  check_table(block_table);
   const int64_t B = slot_ids.size(0);
   TORCH_CHECK(kv_lens.dim() == 1 && kv_lens.size(0) == B, "kv_lens must be (B,)");
   TORCH_CHECK(cu_seqlens.dim() == 1 && cu_seqlens.size(0) == B + 1, "cu_seqlens must be (B+1,)");
@@ -122,14 +141,18 @@ at::Tensor gqa_mixed_attention(const at::Tensor& q, const at::Tensor& k, const a
                                                     q.get_device());
   at::Tensor ws = at::empty({static_cast<int64_t>((ws_bytes + 3) / sizeof(float))},
                             q.options().dtype(at::kFloat));
-  const int st = cie_mixed_attention(
-      q.data_ptr(), k.data_ptr(), v.data_ptr(), max_seqlen, cu_seqlens.data_ptr<int64_t>(),
-      kv_lens.data_ptr<int64_t>(), slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(),
-      o.data_ptr(), ws.data_ptr(), ws_bytes, static_cast<int>(B),
-      q.size(1), static_cast<int>(q.size(2)), static_cast<int>(k.size(1)),
-      static_cast<int>(q.size(3)), static_cast<int>(k.size(2)), k.size(0), block_table.size(0),
-      block_table.stride(0), k.stride(0), k.stride(1), 0,
-      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  const int st = with_table(
+      block_table,
+      [&](auto fn, auto* table) {
+        return fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), max_seqlen, cu_seqlens.data_ptr<int64_t>(),
+          kv_lens.data_ptr<int64_t>(), slot_ids.data_ptr<int64_t>(), table,
+          o.data_ptr(), ws.data_ptr(), ws_bytes, static_cast<int>(B),
+          q.size(1), static_cast<int>(q.size(2)), static_cast<int>(k.size(1)),
+          static_cast<int>(q.size(3)), static_cast<int>(k.size(2)), k.size(0), block_table.size(0),
+          block_table.stride(0), k.stride(0), k.stride(1), 0,
+          reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+      },
+      cie_mixed_attention, cie_mixed_attention_bt32);
   check_status(st, "gqa_mixed_attention");
   return o;
 }
@@ -156,20 +179,24 @@ void kv_decode_update(at::Tensor& k_cache, at::Tensor& v_cache, const at::Tensor
   check_update_src(k_cache, v_cache, k_new, v_new);
   check_i64(lens, "lens");
   check_i64(slot_ids, "slot_ids");
-  check_i64(block_table, "block_table");
+  check_table(block_table);
   TORCH_CHECK(block_table.dim() == 2 && block_table.stride(1) == 1, "block_table must be 2-D");
   TORCH_CHECK(k_new.size(1) == slot_ids.size(0), "one new row per slot id");
   TORCH_CHECK(lens.is_contiguous() && slot_ids.is_contiguous(), "lens / slot_ids contiguous");
   c10::cuda::CUDAGuard guard(k_cache.device());
-  const int st = cie_kv_decode_update(
-      k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr<int64_t>(),
-      slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(), k_new.data_ptr(),
-      v_new.data_ptr(), static_cast<int>(slot_ids.size(0)), static_cast<int>(k_cache.size(1)),
-      static_cast<int>(k_cache.size(3)), static_cast<int>(k_cache.size(2)), k_cache.size(0),
-      lens.size(0) < block_table.size(0) ? lens.size(0) : block_table.size(0),
-      block_table.stride(0), k_cache.stride(0), k_cache.stride(1), k_new.stride(1),
-      k_new.stride(2), v_new.stride(1), v_new.stride(2),
-      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  const int st = with_table(
+      block_table,
+      [&](auto fn, auto* table) {
+        return fn(k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr<int64_t>(),
+          slot_ids.data_ptr<int64_t>(), table, k_new.data_ptr(),
+          v_new.data_ptr(), static_cast<int>(slot_ids.size(0)), static_cast<int>(k_cache.size(1)),
+          static_cast<int>(k_cache.size(3)), static_cast<int>(k_cache.size(2)), k_cache.size(0),
+          lens.size(0) < block_table.size(0) ? lens.size(0) : block_table.size(0),
+          block_table.stride(0), k_cache.stride(0), k_cache.stride(1), k_new.stride(1),
+          k_new.stride(2), v_new.stride(1), v_new.stride(2),
+          reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+      },
+      cie_kv_decode_update, cie_kv_decode_update_bt32);
   check_status(st, "kv_decode_update");
 }
 
@@ -228,22 +255,26 @@ at::Tensor rope_kv_decode_update(const at::Tensor& qkv, const at::Tensor& cos,
   check_rope_src(qkv, cos, sin, k_cache, v_cache);
   check_i64(lens, "lens");
   check_i64(slot_ids, "slot_ids");
-  check_i64(block_table, "block_table");
+  check_table(block_table);
   TORCH_CHECK(block_table.dim() == 2 && block_table.stride(1) == 1, "block_table must be 2-D");
   TORCH_CHECK(slot_ids.dim() == 1 && slot_ids.size(0) == qkv.size(1), "one token per slot id");
   TORCH_CHECK(lens.is_contiguous() && slot_ids.is_contiguous(), "lens / slot_ids contiguous");
   c10::cuda::CUDAGuard guard(qkv.device());
   at::Tensor q = rope_out(qkv, k_cache);
-  const int st = cie_rope_kv_decode_update(
-      qkv.data_ptr(), qkv.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1),
-      q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr<int64_t>(),
-      slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(),
-      static_cast<int>(slot_ids.size(0)), static_cast<int>(q.size(2)),
-      static_cast<int>(k_cache.size(1)), static_cast<int>(k_cache.size(3)),
-      static_cast<int>(k_cache.size(2)), k_cache.size(0),
-      lens.size(0) < block_table.size(0) ? lens.size(0) : block_table.size(0),
-      block_table.stride(0), k_cache.stride(0), k_cache.stride(1),
-      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  const int st = with_table(
+      block_table,
+      [&](auto fn, auto* table) {
+        return fn(qkv.data_ptr(), qkv.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1),
+          q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr<int64_t>(),
+          slot_ids.data_ptr<int64_t>(), table,
+          static_cast<int>(slot_ids.size(0)), static_cast<int>(q.size(2)),
+          static_cast<int>(k_cache.size(1)), static_cast<int>(k_cache.size(3)),
+          static_cast<int>(k_cache.size(2)), k_cache.size(0),
+          lens.size(0) < block_table.size(0) ? lens.size(0) : block_table.size(0),
+          block_table.stride(0), k_cache.stride(0), k_cache.stride(1),
+          reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+      },
+      cie_rope_kv_decode_update, cie_rope_kv_decode_update_bt32);
   check_status(st, "rope_kv_decode_update");
   return q;
 }
@@ -278,7 +309,7 @@ at::Tensor rope_kv_decode_attention(const at::Tensor& qkv, const at::Tensor& cos
   check_rope_src(qkv, cos, sin, k_cache, v_cache);
   check_i64(lens, "lens");
   check_i64(slot_ids, "slot_ids");
-  check_i64(block_table, "block_table");
+  check_table(block_table);
   TORCH_CHECK(block_table.dim() == 2 && block_table.stride(1) == 1 &&
                   block_table.size(1) == k_cache.size(0),
               "block_table must be (n_slots, n_pages)");
@@ -296,16 +327,20 @@ at::Tensor rope_kv_decode_attention(const at::Tensor& qkv, const at::Tensor& cos
   at::Tensor ws;
   if (ws_bytes > 0)
     ws = at::empty({static_cast<int64_t>(ws_bytes / sizeof(float))}, qkv.options().dtype(at::kFloat));
-  const int st = cie_rope_kv_decode_attention(
-      qkv.data_ptr(), qkv.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1),
-      k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr<int64_t>(),
-      slot_ids.data_ptr<int64_t>(), block_table.data_ptr<int64_t>(), o.data_ptr(),
-      ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, static_cast<int>(B), hq,
-      static_cast<int>(k_cache.size(1)), static_cast<int>(k_cache.size(3)),
-      static_cast<int>(k_cache.size(2)), k_cache.size(0),
-      lens.size(0) < block_table.size(0) ? lens.size(0) : block_table.size(0),
-      block_table.stride(0), k_cache.stride(0), k_cache.stride(1), S,
-      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  const int st = with_table(
+      block_table,
+      [&](auto fn, auto* table) {
+        return fn(qkv.data_ptr(), qkv.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1),
+          k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr<int64_t>(),
+          slot_ids.data_ptr<int64_t>(), table, o.data_ptr(),
+          ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, static_cast<int>(B), hq,
+          static_cast<int>(k_cache.size(1)), static_cast<int>(k_cache.size(3)),
+          static_cast<int>(k_cache.size(2)), k_cache.size(0),
+          lens.size(0) < block_table.size(0) ? lens.size(0) : block_table.size(0),
+          block_table.stride(0), k_cache.stride(0), k_cache.stride(1), S,
+          reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+      },
+      cie_rope_kv_decode_attention, cie_rope_kv_decode_attention_bt32);
   check_status(st, "rope_kv_decode_attention");
   return o;
 }

@@ -2,7 +2,8 @@
 
 Layout per layer: ``(n_pages, H_kv, page_size, head_dim)`` for K and for V,
 ``n_pages = ceil(max_cache_len / page_size)``; ``lens (n_slots,)`` int64,
-``block_table (n_slots, n_pages)`` int64 and ``last_generated (n_slots,)``.
+``block_table (n_slots, n_pages)`` int64 (or int32, ``block_table_dtype``) and
+``last_generated (n_slots,)``.
 Slot 0 and page 0 are padding. ``decode_update`` / ``mixed_update`` are the
 mutating ops ``inference::kv_decode_update`` / ``inference::kv_mixed_update``
 (one CUDA launch each for K and V of every token and head); Dynamo sees them
@@ -23,7 +24,13 @@ _mixed_update = torch.ops.inference.kv_mixed_update.default
 
 class KVStorage:
 
-    def __init__(self, config, max_cache_len, page_size, n_slots, device, dtype):
+    def __init__(self, config, max_cache_len, page_size, n_slots, device, dtype, *,
+                 block_table_dtype=torch.int64):
+        """``block_table_dtype`` (keyword only, not in the reference): int64, the
+        reference's layout, or int32 (half the bytes per entry; every op of this
+        package takes either)."""
+        if block_table_dtype not in (torch.int64, torch.int32):
+            raise ValueError(f"block_table_dtype must be int64 or int32, not {block_table_dtype}")
         self.config = config
         self.max_cache_len = max_cache_len
         self.page_size = page_size
@@ -46,7 +53,8 @@ class KVStorage:
         self.values = [torch.zeros(shape, device=device, dtype=dtype)
                        for _ in range(self.num_layers)]
         self.lens = torch.zeros((n_slots,), dtype=torch.long, device=device)
-        self.block_table = torch.zeros((n_slots, self.n_pages), dtype=torch.long, device=device)
+        self.block_table = torch.zeros((n_slots, self.n_pages), dtype=block_table_dtype,
+                                       device=device)
         self.last_generated = torch.zeros((n_slots,), dtype=torch.long, device=device)
 
     def mixed_update(self, layer_num: int, pages: torch.Tensor, offsets: torch.Tensor,

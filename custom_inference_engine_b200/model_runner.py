@@ -128,7 +128,8 @@ class PagedRunner:
     """
 
     def __init__(self, model, max_cache_len: int, n_slots: int, page_seed: int = 0,
-                 token_budget: int = 2048, fused_body: bool = True, mixed_graphs: bool = True):
+                 token_budget: int = 2048, fused_body: bool = True, mixed_graphs: bool = True,
+                 block_table_dtype=torch.int64):
         from .attn.core import use_cuda_attention
         from .kv_cache.storage import KVStorage
 
@@ -137,7 +138,7 @@ class PagedRunner:
         self.device = next(model.parameters()).device
         self.dtype = next(model.parameters()).dtype
         self.kv = KVStorage(model.config, max_cache_len, PAGE_SIZE, n_slots, self.device,
-                            self.dtype)
+                            self.dtype, block_table_dtype=block_table_dtype)
         g = torch.Generator().manual_seed(page_seed)
         self.free_pages = (torch.randperm(self.kv.n_pages - 1, generator=g) + 1).tolist()
         self.token_budget = token_budget

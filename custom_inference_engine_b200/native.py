@@ -63,13 +63,19 @@ SIGNATURES = {
                                              c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_int,
                                              c_int, c_int, c_int, c_int, c_i64, c_i64, c_i64,
                                              c_i64, c_i64, c_int, c_ptr]),
+}
+# the int32-block-table variants take the same arguments
+for _name in ("cie_decode_attention", "cie_mixed_attention", "cie_kv_decode_update",
+              "cie_rope_kv_decode_update", "cie_rope_kv_decode_attention"):
+    SIGNATURES[_name + "_bt32"] = SIGNATURES[_name]
+SIGNATURES.update({
     # include/cie_model_ops.h
     "cie_rms_norm": (c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_int, c_i64, c_i64, c_i64,
                              ctypes.c_float, c_ptr]),
     "cie_silu_mul": (c_int, [c_ptr, c_ptr, c_ptr, c_i64, c_int, c_i64, c_i64, c_i64, c_ptr]),
     "cie_argmax_workspace_bytes": (c_size, [c_i64]),
     "cie_argmax_rows": (c_int, [c_ptr, c_i64, c_int, c_i64, c_ptr, c_ptr, c_size, c_ptr]),
-}
+})
 
 CIE_OK = 0
 STATUS = {

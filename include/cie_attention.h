@@ -259,6 +259,56 @@ int cie_rope_kv_decode_attention(const void* qkv, int64_t qkv_tok_stride, const 
                                  int64_t n_slots, int64_t bt_stride, int64_t cache_page_stride,
                                  int64_t cache_head_stride, int num_splits, cie_stream_t stream);
 
+/* ---- int32 block table ------------------------------------------------------
+ * The reference keeps the block table as int64 (kv_cache/storage.py:52-56) and
+ * every entry point above takes it so. These variants take the same table as
+ * int32 page ids (half the bytes per entry; page ids must be < 2^31, which the
+ * n_pages check already requires) and are otherwise identical -- same
+ * arguments, statuses and results, bit for bit. The torch ops dispatch to them
+ * when block_table has dtype int32.
+ */
+int cie_decode_attention_bt32(const void* q, const void* k, const void* v, const int64_t* lens,
+                              const int64_t* slot_ids, const int32_t* block_table, void* o,
+                              void* workspace, size_t workspace_bytes, int batch, int num_q_heads,
+                              int num_kv_heads, int head_dim, int page_size, int64_t n_pages,
+                              int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
+                              int64_t kv_head_stride, int num_splits, cie_stream_t stream);
+
+int cie_mixed_attention_bt32(const void* q, const void* k, const void* v, int64_t max_seqlen,
+                             const int64_t* cu_seqlens, const int64_t* kv_lens,
+                             const int64_t* slot_ids, const int32_t* block_table, void* o,
+                             void* workspace, size_t workspace_bytes, int batch,
+                             int64_t total_tokens, int num_q_heads, int num_kv_heads,
+                             int head_dim, int page_size, int64_t n_pages, int64_t n_slots,
+                             int64_t bt_stride, int64_t kv_page_stride, int64_t kv_head_stride,
+                             int num_splits, cie_stream_t stream);
+
+int cie_kv_decode_update_bt32(void* k_cache, void* v_cache, const int64_t* lens,
+                              const int64_t* slot_ids, const int32_t* block_table,
+                              const void* k_new, const void* v_new, int batch, int num_kv_heads,
+                              int head_dim, int page_size, int64_t n_pages, int64_t n_slots,
+                              int64_t bt_stride, int64_t cache_page_stride,
+                              int64_t cache_head_stride, int64_t k_tok_stride,
+                              int64_t k_head_stride, int64_t v_tok_stride,
+                              int64_t v_head_stride, cie_stream_t stream);
+
+int cie_rope_kv_decode_update_bt32(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                                   const void* sin, int64_t cs_tok_stride, void* q_out,
+                                   void* k_cache, void* v_cache, const int64_t* lens,
+                                   const int64_t* slot_ids, const int32_t* block_table, int batch,
+                                   int num_q_heads, int num_kv_heads, int head_dim,
+                                   int page_size, int64_t n_pages, int64_t n_slots,
+                                   int64_t bt_stride, int64_t cache_page_stride,
+                                   int64_t cache_head_stride, cie_stream_t stream);
+
+int cie_rope_kv_decode_attention_bt32(
+    const void* qkv, int64_t qkv_tok_stride, const void* cos, const void* sin,
+    int64_t cs_tok_stride, void* k_cache, void* v_cache, const int64_t* lens,
+    const int64_t* slot_ids, const int32_t* block_table, void* o, void* workspace,
+    size_t workspace_bytes, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+    int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride, int64_t cache_page_stride,
+    int64_t cache_head_stride, int num_splits, cie_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -193,3 +193,17 @@ def test_noalloc_checks_arguments_before_its_scratch_limit():
     assert noalloc(d=128, splits=400) == -2
     assert noalloc(k=(1 << 21) + 2, splits=400) == -4
     assert noalloc(splits=400) == -5               # valid, but 4 x 400 splits > 4 MiB
+
+
+def test_bt32_variants_check_arguments_like_the_int64_ones():
+    """The int32-block-table entry points reject what the int64 ones reject."""
+    lib = native.lib()
+    p = 1 << 20
+    args = [p, p, p, p, p, p, p, None, 0, 4, 14, 2, 64, 16, 100, 5, 100, 2048, 1024]
+    assert lib.cie_decode_attention_bt32(None, *args[1:], 1, None) == -1
+    bad = list(args)
+    bad[12] = 128   # head_dim
+    assert lib.cie_decode_attention_bt32(*bad, 1, None) == -2
+    assert lib.cie_decode_attention_bt32(*args, 4, None) == -5   # split path without workspace
+    assert lib.cie_kv_decode_update_bt32(p, p, p, p, None, p, p, 4, 2, 64, 16, 10, 3, 10, 2048,
+                                         1024, 1152, 64, 1152, 64, None) == -1
