@@ -177,3 +177,20 @@ def rope_kv_decode_attention(qkv, cos, sin, k_cache, v_cache, lens, slot_ids, bl
         k_cache.stride(1), S, native.stream_ptr(stream))
     native.check(st, "cie_rope_kv_decode_attention")
     return out
+
+
+def lm_head_argmax(hidden, weight, logits: bool = False, stream=None):
+    """cie_lm_head_argmax: greedy tokens (int64, one per hidden row) of
+    hidden (B, H) . weight (V, H)^T; with ``logits`` also the fp16 logits (B, V)."""
+    B, H = hidden.shape
+    V = weight.shape[0]
+    dev = hidden.device
+    tokens = torch.empty(B, dtype=torch.int64, device=dev)
+    out = torch.empty(B, V, dtype=torch.float16, device=dev) if logits else None
+    need = int(native.lib().cie_lm_head_argmax_workspace_bytes(B, V, dev.index or 0))
+    ws = torch.empty(max(need // 8, 1), dtype=torch.int64, device=dev)
+    st = native.lib().cie_lm_head_argmax(
+        _p(hidden), hidden.stride(0), _p(weight), weight.stride(0), B, H, V, _p(out), V,
+        _p(tokens), _p(ws), ws.numel() * 8, native.stream_ptr(stream))
+    native.check(st, "cie_lm_head_argmax")
+    return (tokens, out) if logits else tokens

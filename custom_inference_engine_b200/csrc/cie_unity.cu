@@ -5,5 +5,6 @@
 #include "decode_attention.cu"
 #include "decode_noalloc.cu"
 #include "kv_update.cu"
+#include "lm_head.cu"
 #include "mixed_attention.cu"
 #include "rope_kv.cu"

@@ -426,6 +426,31 @@ at::Tensor argmax_rows(const at::Tensor& x) {
   return out;
 }
 
+// tokens = argmax(hidden . weight^T) over the vocabulary, in one pass over the
+// weight (cie_lm_head_argmax); hidden (..., H) with a contiguous last dim.
+at::Tensor lm_head_argmax(const at::Tensor& hidden, const at::Tensor& weight) {
+  check_rows(hidden, "hidden");
+  check_rows(weight, "weight");
+  TORCH_CHECK(weight.dim() == 2 && weight.size(1) == hidden.size(-1),
+              "weight must be (vocab, hidden_size)");
+  c10::cuda::CUDAGuard guard(hidden.device());
+  std::vector<int64_t> shape(hidden.sizes().begin(), hidden.sizes().end() - 1);
+  at::Tensor out = at::empty(shape, hidden.options().dtype(at::kLong));
+  const int64_t rows = hidden.numel() / std::max<int64_t>(hidden.size(-1), 1);
+  if (rows == 0) return out;
+  const size_t ws_bytes =
+      cie_lm_head_argmax_workspace_bytes(static_cast<int>(rows), weight.size(0), hidden.get_device());
+  at::Tensor ws = at::empty({static_cast<int64_t>(std::max<size_t>(ws_bytes, 8) / 8)},
+                            hidden.options().dtype(at::kLong));
+  const int st = cie_lm_head_argmax(
+      hidden.data_ptr(), row_stride(hidden), weight.data_ptr(), weight.stride(0),
+      static_cast<int>(rows), static_cast<int>(hidden.size(-1)), weight.size(0), nullptr, 0,
+      out.data_ptr<int64_t>(), ws.data_ptr(), ws_bytes,
+      reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+  check_status(st, "lm_head_argmax");
+  return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(inference, m) {
@@ -457,6 +482,7 @@ TORCH_LIBRARY(inference, m) {
   m.def("add_rms_norm(Tensor(a!) residual, Tensor delta, Tensor weight, float eps) -> Tensor");
   m.def("silu_and_mul(Tensor gate_up) -> Tensor");
   m.def("argmax_rows(Tensor x) -> Tensor");
+  m.def("lm_head_argmax(Tensor hidden, Tensor weight) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(inference, CUDA, m) {
@@ -472,4 +498,5 @@ TORCH_LIBRARY_IMPL(inference, CUDA, m) {
   m.impl("add_rms_norm", &add_rms_norm);
   m.impl("silu_and_mul", &silu_and_mul);
   m.impl("argmax_rows", &argmax_rows);
+  m.impl("lm_head_argmax", &lm_head_argmax);
 }

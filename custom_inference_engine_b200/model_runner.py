@@ -129,7 +129,7 @@ class PagedRunner:
 
     def __init__(self, model, max_cache_len: int, n_slots: int, page_seed: int = 0,
                  token_budget: int = 2048, fused_body: bool = True, mixed_graphs: bool = True,
-                 block_table_dtype=torch.int64):
+                 block_table_dtype=torch.int64, fused_lm_head: bool = True):
         from .attn.core import use_cuda_attention
         from .kv_cache.storage import KVStorage
 
@@ -150,6 +150,10 @@ class PagedRunner:
         # mixed_graphs: mixed passes replay a CUDA graph per token bucket (the
         # reference's FullMixedModule); False runs them eagerly
         self.use_mixed_graphs = mixed_graphs and self.device.type == "cuda"
+        # fused_lm_head: decode steps take the greedy token from one pass over the
+        # lm_head weight (inference::lm_head_argmax) and keep no logits; False
+        # runs the lm_head GEMM, keeps the logits and takes their argmax
+        self.fused_lm_head = fused_lm_head
         self.mixed_buckets = sorted({b for b in MIXED_TOKEN_BUCKETS if b < token_budget}
                                     | {token_budget})
         self._mixed_graphs = {}
@@ -298,7 +302,9 @@ class PagedRunner:
 class DecodeGraph:
     """One greedy decode step for a fixed batch of slots: the tokens of the
     previous step in, the next tokens out (``tokens``, device (B,)), every slot
-    one position longer. Captured in a CUDA graph unless ``capture`` is False."""
+    one position longer. Captured in a CUDA graph unless ``capture`` is False.
+    ``logits`` holds the step's logits only when the runner's ``fused_lm_head``
+    is off."""
 
     def __init__(self, runner: PagedRunner, slots, first_tokens, capture: bool = True):
         from .attn.metadata import AttentionMetadata
@@ -335,8 +341,12 @@ class DecodeGraph:
         ids = self.tokens.view(1, -1)
         pos = kv.lens[self.md.slot_ids].view(1, -1)
         hidden = self.runner._hidden(ids, pos, self.md)
-        self.logits = self.runner.model.lm_head(hidden[0])
-        self.tokens.copy_(torch.ops.inference.argmax_rows(self.logits))
+        lm_head = self.runner.model.lm_head
+        if self.runner.fused_lm_head and lm_head.bias is None:
+            self.tokens.copy_(torch.ops.inference.lm_head_argmax(hidden[0], lm_head.weight))
+        else:
+            self.logits = lm_head(hidden[0])
+            self.tokens.copy_(torch.ops.inference.argmax_rows(self.logits))
         kv.decode_advance(self.md.slot_ids)
 
     def step(self) -> torch.Tensor:

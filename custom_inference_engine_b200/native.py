@@ -75,6 +75,9 @@ SIGNATURES.update({
     "cie_silu_mul": (c_int, [c_ptr, c_ptr, c_ptr, c_i64, c_int, c_i64, c_i64, c_i64, c_ptr]),
     "cie_argmax_workspace_bytes": (c_size, [c_i64]),
     "cie_argmax_rows": (c_int, [c_ptr, c_i64, c_int, c_i64, c_ptr, c_ptr, c_size, c_ptr]),
+    "cie_lm_head_argmax_workspace_bytes": (c_size, [c_int, c_i64, c_int]),
+    "cie_lm_head_argmax": (c_int, [c_ptr, c_i64, c_ptr, c_i64, c_int, c_int, c_i64, c_ptr,
+                                   c_i64, c_ptr, c_ptr, c_size, c_ptr]),
 })
 
 CIE_OK = 0
@@ -188,6 +191,10 @@ def _register_fakes() -> None:
     @torch.library.register_fake("inference::argmax_rows")
     def _argmax_fake(x):
         return x.new_empty(x.shape[:-1], dtype=torch.long)
+
+    @torch.library.register_fake("inference::lm_head_argmax")
+    def _lm_head_argmax_fake(hidden, weight):
+        return hidden.new_empty(hidden.shape[:-1], dtype=torch.long)
 
     @torch.library.register_fake("inference::silu_and_mul")
     def _silu_mul_fake(gate_up):

@@ -59,6 +59,28 @@ size_t cie_argmax_workspace_bytes(int64_t rows);
 int cie_argmax_rows(const void* x, int64_t rows, int n, int64_t stride, int64_t* out,
                     void* workspace, size_t workspace_bytes, cie_stream_t stream);
 
+/*
+ * The greedy token after the last-token lm_head, in one pass over the weight
+ * (the lm_head GEMM + argmax of scheduler/decode_module.py:103-107 and
+ * scheduler/mixed_module.py:58-65): tokens[b] = argmax over v of
+ * fp16(hidden[b] . weight[v]), with cie_argmax_rows' semantics (first index of
+ * the maximum, NaN largest). hidden (batch, hidden_size) and weight (vocab,
+ * hidden_size) fp16 at the given row strides (elements; rows 16-byte aligned);
+ * hidden_size a multiple of 64 up to 1024; vocab < 2^30. `logits` (optional,
+ * may be NULL) receives the fp16 logits (batch, vocab) at logits_stride; they
+ * are the tensor core's fp32 dot products rounded once to fp16, as a fp16 GEMM
+ * with fp32 accumulation returns them (the summation order may differ from
+ * another GEMM's in the last fp32 bit). Batches above 64 run in slices of 64
+ * rows (one pass over the weight each). `workspace`:
+ * cie_lm_head_argmax_workspace_bytes(batch, vocab, device) bytes, 16-byte
+ * aligned, no initialisation.
+ */
+size_t cie_lm_head_argmax_workspace_bytes(int batch, int64_t vocab, int device);
+int cie_lm_head_argmax(const void* hidden, int64_t hidden_stride, const void* weight,
+                       int64_t weight_stride, int batch, int hidden_size, int64_t vocab,
+                       void* logits, int64_t logits_stride, int64_t* tokens, void* workspace,
+                       size_t workspace_bytes, cie_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

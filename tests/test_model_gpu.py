@@ -132,7 +132,8 @@ def test_logits_follow_the_reference_engine(cuda_device):
     cfg = MR.qwen2_config(num_hidden_layers=2, vocab_size=4096, intermediate_size=2048)
     model = MR.random_qwen2(cfg, seed=int(g["seed"]), device="cpu").to(dev)
     B = len(prompts)
-    runner = MR.PagedRunner(model, max_cache_len=1024, n_slots=B + 1, token_budget=1024)
+    runner = MR.PagedRunner(model, max_cache_len=1024, n_slots=B + 1, token_budget=1024,
+                            fused_lm_head=False)   # the test reads every step's logits
     slots = list(range(1, B + 1))
     for s in slots:
         runner.admit(s, 160)
