@@ -590,6 +590,35 @@ def run_sweep(args, dev):
         print(json.dumps(p), flush=True)
 
 
+def lm_head_line(dev, batch: int = 64):
+    """The last-token lm_head + argmax of a decode step at the Qwen2.5-0.5B
+    shape (hidden 896, vocab 151936, ``batch`` rows): the fused one-pass
+    kernel (inference::lm_head_argmax) against cuBLAS's GEMM followed by this
+    package's argmax, each timed with a cold L2 (``graph_time_cold``). HBM
+    roofline: the weight, the hidden rows and the tokens."""
+    from custom_inference_engine_b200.attn import core  # noqa: F401  (loads the ops)
+    V, H = 151936, 896
+    g = torch.Generator(device=dev).manual_seed(9)
+    w = (torch.randn(V, H, generator=g, device=dev) * 0.02).half()
+    h = torch.randn(batch, H, generator=g, device=dev).half()
+    ops = torch.ops.inference
+    fused = lambda: ops.lm_head_argmax(h, w)
+    gemm = lambda: ops.argmax_rows(torch.nn.functional.linear(h, w))
+    assert torch.equal(fused(), ops.lm_head_argmax(h, w))
+    for f in (fused, gemm):
+        for _ in range(3):
+            f()
+    ms_f = graph_time_cold(fused, dev)
+    ms_g = graph_time_cold(gemm, dev)
+    nbytes = V * H * 2 + batch * H * 2 + batch * 8
+    peak, kind = measured_peak_gbs()
+    gbs = nbytes / (ms_f / 1e3) / 1e9
+    return {"batch": batch, "vocab": V, "hidden": H, "fused_us": ms_f * 1e3,
+            "gemm_plus_argmax_us": ms_g * 1e3, "algorithmic_bytes": nbytes,
+            "fused_gbs": gbs, "frac_of_hbm": gbs / peak, "peak_source": f"{kind} hbm_gbs",
+            "timing": "cold L2, CUDA graph of 20 calls minus the same graph without them"}
+
+
 def serving_line(args, rank, world, dev):
     """Qwen2.5-0.5B-shape model through the paged ops (every rank its own replica).
 
@@ -955,6 +984,7 @@ def run_ours(args, rank, world, local):
         if world == 1 and not args.no_sweep:
             result["sweep"], ref = sweep_with_reference(dev)
             result["reference_triton"] = ref
+            result["lm_head"] = lm_head_line(dev)
         if not args.no_cpu_baseline and world == 1:
             gbs, cores, sample = cpu_oracle_rate(L, args.cpu_seconds)
             result["cpu_baseline"] = {"value": gbs, "unit": UNIT, "cores": cores, "kind": "port",
