@@ -93,6 +93,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-sweep", action="store_true",
                     help="skip the config-2 / config-5 sweep and the reference Triton timings "
                          "(run at N=1 only)")
+    ap.add_argument("--lm-head-only", action="store_true",
+                    help="print only the fused lm_head + argmax line (profiling)")
     ap.add_argument("--sweep", action="store_true",
                     help="print one JSON line per decode sweep point (configs 2 and 5) "
                          "instead of the benchmark line")
@@ -1000,6 +1002,9 @@ def main(argv=None):
             if rank == 0:
                 run_sweep(args, torch.device("cuda", torch.cuda.current_device()))
             res = None
+        elif args.lm_head_only:
+            res = lm_head_line(torch.device("cuda", torch.cuda.current_device())) \
+                if rank == 0 else None
         elif args.impl == "reference":
             res = run_reference(args, rank, world)
         else:

@@ -36,6 +36,7 @@ gqa_mixed_attention_op = torch.ops.inference.gqa_mixed_attention.default
 rope_kv_decode_update_op = torch.ops.inference.rope_kv_decode_update.default
 rope_kv_mixed_update_op = torch.ops.inference.rope_kv_mixed_update.default
 rope_kv_decode_attention_op = torch.ops.inference.rope_kv_decode_attention.default
+rope_kv_mixed_attention_op = torch.ops.inference.rope_kv_mixed_attention.default
 _gqa_decode_attention_splits = torch.ops.inference.gqa_decode_attention_splits.default
 
 # The reference tunes Triton tiles here (attn/core.py:114-116). The CUDA decode
@@ -107,8 +108,13 @@ class TritonQwen2Attention(torch.nn.Module):
     ``mixed_update`` and the attention op. ``fuse_decode_attention = False``
     splits the decode pass into the RoPE + KV launch and the attention op;
     ``fuse_rope = False`` restores the reference's sequence (HF RoPE, then
-    ``kv_manager``'s update methods). Without ``kv_manager`` it defers to the
-    wrapped HF module.
+    ``kv_manager``'s update methods). A mixed pass whose metadata has
+    ``fuse_mixed_attention`` set is one call too
+    (``inference::rope_kv_mixed_attention``); metadata written by the
+    reference's modules never sets it, because the reference's piecewise
+    backend splits the graph at ``inference::gqa_mixed_attention`` nodes
+    (piecewise/utils.py:5-23), which the one-call form does not contain.
+    Without ``kv_manager`` it defers to the wrapped HF module.
     """
 
     fuse_rope = True
@@ -154,6 +160,19 @@ class TritonQwen2Attention(torch.nn.Module):
             o = rope_kv_decode_attention_op(qkv, cos, sin, kv_manager.keys[layer],
                                             kv_manager.values[layer], kv_manager.lens,
                                             metadata.slot_ids, kv_manager.block_table)
+            return self.original.o_proj(o.reshape(1, total_T, self.num_heads * self.head_dim)), None
+        if (self.fuse_rope and not metadata.full_decode
+                and getattr(metadata, "fuse_mixed_attention", False)):
+            # RoPE, K/V write and mixed attention: one call
+            lens = getattr(metadata, "attn_lens", None)
+            if lens is None:
+                lens = kv_manager.lens[metadata.slot_ids]
+            o = rope_kv_mixed_attention_op(qkv, cos, sin, kv_manager.keys[layer],
+                                           kv_manager.values[layer], metadata.pages,
+                                           metadata.offsets, max_seqlen=metadata.max_seqlen,
+                                           cu_seqlens=metadata.cu_seqlens, kv_lens=lens,
+                                           slot_ids=metadata.slot_ids,
+                                           block_table=kv_manager.block_table)
             return self.original.o_proj(o.reshape(1, total_T, self.num_heads * self.head_dim)), None
         if self.fuse_rope:
             if metadata.full_decode:

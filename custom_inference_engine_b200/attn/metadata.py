@@ -29,6 +29,11 @@ class AttentionMetadata:
         # (decode: lens[slot_ids] + 1, mixed: lens[slot_ids]) computed once by
         # the caller; when None every layer computes them from the KV storage.
         self.attn_lens = None
+        # Optional, not in the reference: a mixed pass with this set runs its
+        # RoPE, K/V write and attention as one call (rope_kv_mixed_attention);
+        # left False, the pass keeps the reference's gqa_mixed_attention op,
+        # which the reference's piecewise splitter cuts the graph at.
+        self.fuse_mixed_attention = False
 
     def prepare_full_graph(self, batch_size: int):
         """Fixed-size slot / cu_seqlens buffers for a captured CUDA graph."""

@@ -194,3 +194,26 @@ def lm_head_argmax(hidden, weight, logits: bool = False, stream=None):
         _p(tokens), _p(ws), ws.numel() * 8, native.stream_ptr(stream))
     native.check(st, "cie_lm_head_argmax")
     return (tokens, out) if logits else tokens
+
+
+def rope_kv_mixed_attention(qkv, cos, sin, k_cache, v_cache, pages, offsets, max_seqlen: int,
+                            cu_seqlens, kv_lens, slot_ids, block_table, out=None,
+                            num_splits: int = 0, stream=None):
+    """cie_rope_kv_mixed_attention: token t's rotated k and its v written to
+    (pages[t], offsets[t]), then the mixed attention of the pass over the pages
+    (q rotated on the way); returns o (1, T, H_q, D)."""
+    out, hq = _rope_q_out(qkv, k_cache, out)
+    B, T = slot_ids.shape[0], qkv.shape[1]
+    dev = qkv.device
+    need = int(native.lib().cie_rope_kv_mixed_workspace_bytes(B, T, hq, k_cache.shape[1],
+                                                                num_splits, dev.index or 0))
+    ws = torch.empty(max(need // 4, 1) + 1, dtype=torch.float32, device=dev)
+    st = _entry("cie_rope_kv_mixed_attention", block_table)(
+        _p(qkv), qkv.stride(1), _p(cos), _p(sin), cos.stride(1), _p(k_cache), _p(v_cache),
+        _p(pages), _p(offsets), int(max_seqlen), _p(cu_seqlens), _p(kv_lens), _p(slot_ids),
+        _p(block_table), _p(out), _p(ws), ws.numel() * 4, B, T, hq, k_cache.shape[1],
+        k_cache.shape[3], k_cache.shape[2], k_cache.shape[0], block_table.shape[0],
+        block_table.stride(0), k_cache.stride(0), k_cache.stride(1), num_splits,
+        native.stream_ptr(stream))
+    native.check(st, "cie_rope_kv_mixed_attention")
+    return out

@@ -6,5 +6,5 @@
 #include "decode_noalloc.cu"
 #include "kv_update.cu"
 #include "lm_head.cu"
-#include "mixed_attention.cu"
 #include "rope_kv.cu"
+#include "mixed_attention.cu"

@@ -347,7 +347,14 @@ __device__ __forceinline__ int plan_excl_scan(int v, int* s_warp, int& total) {
 // the longest CTAs start first and the short ones fill the tail. Sequences
 // whose rows, slot or length are out of bounds raise a device error here and
 // get no work.
-__global__ void __launch_bounds__(kPlanThreads) mixed_plan_kernel(const Params p) {
+//
+// With `rope_ctas` > 0 (cie_rope_kv_mixed_attention) the grid has that many more
+// CTAs, which apply the rotary embedding to the pass's q and k rows and write
+// k and v to their pages (rope::rope_kv_item, the work of
+// cie_rope_kv_mixed_update) while CTA 0 plans; the attention grid waits for the
+// whole grid, so it reads the rotated q and the written pages.
+__global__ void __launch_bounds__(kPlanThreads)
+    mixed_plan_kernel(const Params p, const rope::Args ra, int rope_ctas) {
   __shared__ int s_pfx[kPlanMaxBatch + 1];  // tile pairs before sequence b
   __shared__ int s_len[kPlanMaxBatch];
   __shared__ int s_kv[kPlanMaxBatch];
@@ -357,6 +364,13 @@ __global__ void __launch_bounds__(kPlanThreads) mixed_plan_kernel(const Params p
   __shared__ int s_cnt[3];  // items, split pairs, records
   // the attention grid may be scheduled now; it waits for this grid to finish
   if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (blockIdx.x > 0) {
+    const int64_t n = rope::work_items(ra);
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x - 1) * kPlanThreads + threadIdx.x; idx < n;
+         idx += static_cast<int64_t>(rope_ctas) * kPlanThreads)
+      rope::rope_kv_item(ra, idx);
+    return;
+  }
   const int tid = threadIdx.x;
   const int B = p.batch;
   const int H = p.num_kv_heads;
@@ -972,17 +986,29 @@ namespace cie {
 namespace mixed {
 
 // Argument checks, tensor maps and the two launches of cie_mixed_attention
-// (and of its int32-block-table variant).
+// (and of its int32-block-table variant). With `rope` (cie_rope_kv_mixed_attention)
+// q is ignored: the planning grid's extra CTAs rotate the pass's q into the
+// workspace tail and write its k / v rows to their pages first.
 int entry(const void* q, const void* k, const void* v, int64_t max_seqlen,
           const int64_t* cu_seqlens, const int64_t* kv_lens, const int64_t* slot_ids,
           BlockTable block_table, void* o, void* workspace, size_t workspace_bytes, int batch,
           int64_t total_tokens, int num_q_heads, int num_kv_heads, int head_dim, int page_size,
           int64_t n_pages, int64_t n_slots, int64_t bt_stride, int64_t kv_page_stride,
-          int64_t kv_head_stride, int num_splits, cie_stream_t stream) {
+          int64_t kv_head_stride, int num_splits, cie_stream_t stream,
+          const rope::Args* rope = nullptr) {
   if (batch < 0 || total_tokens < 0 || max_seqlen < 0)
     return fail(CIE_ERR_INVALID_ARGUMENT, "negative batch / total_tokens / max_seqlen");
+  if (rope != nullptr && total_tokens > 0 && (batch == 0 || max_seqlen == 0)) {
+    // no attention to compute, but the pass's rows still go to their pages
+    rope::Args ra = *rope;
+    ra.q_out = static_cast<__half*>(workspace);
+    if (workspace == nullptr ||
+        workspace_bytes < static_cast<size_t>(total_tokens) * num_q_heads * kD * 2)
+      return fail(CIE_ERR_WORKSPACE, "the rotated q needs workspace");
+    return rope::launch(ra, head_dim, stream);
+  }
   if (batch == 0 || total_tokens == 0 || max_seqlen == 0) return CIE_OK;
-  if (!q || !k || !v || !cu_seqlens || !kv_lens || !slot_ids || !block_table.ptr || !o)
+  if ((!q && !rope) || !k || !v || !cu_seqlens || !kv_lens || !slot_ids || !block_table.ptr || !o)
     return fail(CIE_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (head_dim != kD || page_size != kPage)
     return fail(CIE_ERR_UNSUPPORTED, "head_dim %d / page_size %d (supported: 64 / 16)", head_dim,
@@ -1014,9 +1040,35 @@ int entry(const void* q, const void* k, const void* v, int64_t max_seqlen,
   const int n_sm = sm_count();
   const PlanSizes ps = plan_sizes(batch, total_tokens, num_kv_heads, num_splits, n_sm);
   if (ps.items > 0x7fffffff) return fail(CIE_ERR_OVERFLOW, "too many work items");
-  if (workspace == nullptr || workspace_bytes < ps.bytes)
-    return fail(CIE_ERR_WORKSPACE, "mixed attention needs %zu workspace bytes, got %zu", ps.bytes,
+  size_t need = ps.bytes;
+  rope::Args ra{};
+  int rope_ctas = 0;
+  if (rope != nullptr) {
+    const size_t q_off = round256(ps.bytes);
+    need = q_off + static_cast<size_t>(total_tokens) * num_q_heads * kD * 2;
+    ra = *rope;
+    ra.q_out = workspace ? reinterpret_cast<__half*>(static_cast<uint8_t*>(workspace) + q_off)
+                         : nullptr;
+    ra.k_cache = static_cast<__half*>(const_cast<void*>(k));
+    ra.v_cache = static_cast<__half*>(const_cast<void*>(v));
+    ra.page_stride = kv_page_stride;
+    ra.head_stride = kv_head_stride;
+    ra.num_tokens = total_tokens;
+    ra.hq = num_q_heads;
+    ra.hkv = num_kv_heads;
+    ra.page_size = page_size;
+    ra.n_pages = n_pages;
+    q = ra.q_out;
+  }
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(CIE_ERR_WORKSPACE, "mixed attention needs %zu workspace bytes, got %zu", need,
                 workspace == nullptr ? size_t(0) : workspace_bytes);
+  if (rope != nullptr) {
+    const int st = rope::check(ra, head_dim);
+    if (st != CIE_OK) return st;
+    const int64_t blocks = (rope::work_items(ra) + kPlanThreads - 1) / kPlanThreads;
+    rope_ctas = static_cast<int>(blocks < 4 * n_sm ? blocks : 4 * n_sm);
+  }
   if (!aligned16(workspace)) return fail(CIE_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
 
   CUtensorMap tm_q, tm_k, tm_v;
@@ -1072,7 +1124,7 @@ int entry(const void* q, const void* k, const void* v, int64_t max_seqlen,
   p.num_splits = num_splits;
   p.n_sm = n_sm;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  mixed_plan_kernel<<<1, kPlanThreads, 0, s>>>(p);
+  mixed_plan_kernel<<<1 + rope_ctas, kPlanThreads, 0, s>>>(p, ra, rope_ctas);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "mixed plan launch: %s", cudaGetErrorString(e));
   // one CTA per item (the plan holds at most ps.items; the rest return at
@@ -1123,6 +1175,89 @@ int cie_mixed_attention_bt32(const void* q, const void* k, const void* v, int64_
                            cie::BlockTable{block_table, 0}, o, workspace, workspace_bytes, batch,
                            total_tokens, num_q_heads, num_kv_heads, head_dim, page_size, n_pages,
                            n_slots, bt_stride, kv_page_stride, kv_head_stride, num_splits, stream);
+}
+
+// cie_rope_kv_mixed_attention and its int32-block-table twin.
+static int rope_kv_mixed_attention(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                                   const void* sin, int64_t cs_tok_stride, void* k_cache,
+                                   void* v_cache, const int64_t* pages, const int64_t* offsets,
+                                   int64_t max_seqlen, const int64_t* cu_seqlens,
+                                   const int64_t* kv_lens, const int64_t* slot_ids,
+                                   cie::BlockTable block_table, void* o, void* workspace,
+                                   size_t workspace_bytes, int batch, int64_t total_tokens,
+                                   int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                   int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                                   int64_t cache_page_stride, int64_t cache_head_stride,
+                                   int num_splits, cie_stream_t stream) {
+  using namespace cie;
+  if (total_tokens > 0 && (!pages || !offsets))
+    return fail(CIE_ERR_INVALID_ARGUMENT, "null pages / offsets");
+  rope::Args ra{};
+  ra.qkv = static_cast<const __half*>(qkv);
+  ra.qkv_tok = qkv_tok_stride;
+  ra.cos = static_cast<const __half*>(cos);
+  ra.sin = static_cast<const __half*>(sin);
+  ra.cs_tok = cs_tok_stride;
+  ra.k_cache = static_cast<__half*>(k_cache);
+  ra.v_cache = static_cast<__half*>(v_cache);
+  ra.page_stride = cache_page_stride;
+  ra.head_stride = cache_head_stride;
+  ra.pages = pages;
+  ra.offsets = offsets;
+  ra.num_tokens = total_tokens;
+  ra.hq = num_q_heads;
+  ra.hkv = num_kv_heads;
+  ra.page_size = page_size;
+  ra.n_pages = n_pages;
+  return mixed::entry(nullptr, k_cache, v_cache, max_seqlen, cu_seqlens, kv_lens, slot_ids,
+                      block_table, o, workspace, workspace_bytes, batch, total_tokens,
+                      num_q_heads, num_kv_heads, head_dim, page_size, n_pages, n_slots, bt_stride,
+                      cache_page_stride, cache_head_stride, num_splits, stream, &ra);
+}
+
+size_t cie_rope_kv_mixed_workspace_bytes(int batch, int64_t total_tokens, int num_q_heads,
+                                         int num_kv_heads, int num_splits, int device) {
+  using namespace cie::mixed;
+  if (batch < 0 || total_tokens < 0 || num_kv_heads < 1 || num_q_heads < 1) return 0;
+  const size_t q_bytes = static_cast<size_t>(total_tokens) * num_q_heads * kD * 2;
+  return round256(cie_mixed_workspace_bytes(batch, total_tokens, num_kv_heads, num_splits,
+                                            device)) +
+         q_bytes;
+}
+
+int cie_rope_kv_mixed_attention(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                                const void* sin, int64_t cs_tok_stride, void* k_cache,
+                                void* v_cache, const int64_t* pages, const int64_t* offsets,
+                                int64_t max_seqlen, const int64_t* cu_seqlens,
+                                const int64_t* kv_lens, const int64_t* slot_ids,
+                                const int64_t* block_table, void* o, void* workspace,
+                                size_t workspace_bytes, int batch, int64_t total_tokens,
+                                int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                                int64_t cache_page_stride, int64_t cache_head_stride,
+                                int num_splits, cie_stream_t stream) {
+  return rope_kv_mixed_attention(qkv, qkv_tok_stride, cos, sin, cs_tok_stride, k_cache, v_cache,
+                                 pages, offsets, max_seqlen, cu_seqlens, kv_lens, slot_ids,
+                                 cie::BlockTable{block_table, 1}, o, workspace, workspace_bytes,
+                                 batch, total_tokens, num_q_heads, num_kv_heads, head_dim,
+                                 page_size, n_pages, n_slots, bt_stride, cache_page_stride,
+                                 cache_head_stride, num_splits, stream);
+}
+
+int cie_rope_kv_mixed_attention_bt32(
+    const void* qkv, int64_t qkv_tok_stride, const void* cos, const void* sin,
+    int64_t cs_tok_stride, void* k_cache, void* v_cache, const int64_t* pages,
+    const int64_t* offsets, int64_t max_seqlen, const int64_t* cu_seqlens, const int64_t* kv_lens,
+    const int64_t* slot_ids, const int32_t* block_table, void* o, void* workspace,
+    size_t workspace_bytes, int batch, int64_t total_tokens, int num_q_heads, int num_kv_heads,
+    int head_dim, int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+    int64_t cache_page_stride, int64_t cache_head_stride, int num_splits, cie_stream_t stream) {
+  return rope_kv_mixed_attention(qkv, qkv_tok_stride, cos, sin, cs_tok_stride, k_cache, v_cache,
+                                 pages, offsets, max_seqlen, cu_seqlens, kv_lens, slot_ids,
+                                 cie::BlockTable{block_table, 0}, o, workspace, workspace_bytes,
+                                 batch, total_tokens, num_q_heads, num_kv_heads, head_dim,
+                                 page_size, n_pages, n_slots, bt_stride, cache_page_stride,
+                                 cache_head_stride, num_splits, stream);
 }
 
 }  // extern "C"

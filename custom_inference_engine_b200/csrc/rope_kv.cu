@@ -70,11 +70,16 @@ __device__ __forceinline__ uint4 neg8(uint4 x) {
   return r;
 }
 
-__global__ void rope_kv_kernel(const Args a) {
+// Work items of one launch: one per (token, row, chunk pair).
+__host__ __device__ __forceinline__ int64_t work_items(const Args& a) {
+  return a.num_tokens * (a.hq + 2 * a.hkv) * kHalfChunks;
+}
+
+// Work item `idx` (< work_items(a)): the rotation of one chunk pair of a q or k
+// row, or the copy of a v row's chunk pair, to its destination.
+__device__ __forceinline__ void rope_kv_item(const Args& a, int64_t idx) {
   const int rows = a.hq + 2 * a.hkv;
   const int64_t per_tok = static_cast<int64_t>(rows) * kHalfChunks;
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= a.num_tokens * per_tok) return;
   const int64_t t = idx / per_tok;
   const int row = static_cast<int>((idx % per_tok) / kHalfChunks);
   const int c = static_cast<int>(idx % kHalfChunks);
@@ -130,7 +135,13 @@ __global__ void rope_kv_kernel(const Args a) {
       rope8(x2, x1, ld16(cs + 32 + c * 8), ld16(sn + 32 + c * 8));
 }
 
-int launch(Args a, int head_dim, cie_stream_t stream) {
+__global__ void rope_kv_kernel(const Args a) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx < work_items(a)) rope_kv_item(a, idx);
+}
+
+// Host-side checks of one launch's arguments (CIE_OK or a status).
+int check(const Args& a, int head_dim) {
   if (a.num_tokens < 0) return fail(CIE_ERR_INVALID_ARGUMENT, "negative token count");
   if (a.num_tokens == 0) return CIE_OK;
   if (!a.qkv || !a.cos || !a.sin || !a.q_out || !a.k_cache || !a.v_cache)
@@ -147,7 +158,15 @@ int launch(Args a, int head_dim, cie_stream_t stream) {
       !aligned16(a.qkv) || !aligned16(a.cos) || !aligned16(a.sin) || !aligned16(a.q_out) ||
       !aligned16(a.k_cache) || !aligned16(a.v_cache))
     return fail(CIE_ERR_ALIGNMENT, "all rows must start on 16-byte boundaries");
-  const int64_t threads = a.num_tokens * (a.hq + 2 * a.hkv) * kHalfChunks;
+  return CIE_OK;
+}
+
+int launch(Args a, int head_dim, cie_stream_t stream) {
+  if (a.num_tokens < 0) return fail(CIE_ERR_INVALID_ARGUMENT, "negative token count");
+  if (a.num_tokens == 0) return CIE_OK;
+  const int st = check(a, head_dim);
+  if (st != CIE_OK) return st;
+  const int64_t threads = work_items(a);
   const int block = 256;
   const int64_t grid = (threads + block - 1) / block;
   if (grid > 0x7fffffff) return fail(CIE_ERR_OVERFLOW, "too many tokens");

@@ -302,6 +302,62 @@ at::Tensor rope_kv_mixed_update(const at::Tensor& qkv, const at::Tensor& cos,
   return q;
 }
 
+// rope_kv_mixed_update + gqa_mixed_attention as one call (cie_rope_kv_mixed_attention):
+// the pass's k / v rows are written to their pages and o is returned.
+at::Tensor rope_kv_mixed_attention(const at::Tensor& qkv, const at::Tensor& cos,
+                                   const at::Tensor& sin, at::Tensor& k_cache,
+                                   at::Tensor& v_cache, const at::Tensor& pages,
+                                   const at::Tensor& offsets, c10::SymInt max_seqlen_sym,
+                                   const at::Tensor& cu_seqlens, const at::Tensor& kv_lens,
+                                   const at::Tensor& slot_ids, const at::Tensor& block_table) {
+  const int64_t max_seqlen = max_seqlen_sym.expect_int();
+  check_rope_src(qkv, cos, sin, k_cache, v_cache);
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "k and v must be contiguous");
+  check_i64(pages, "pages");
+  check_i64(offsets, "offsets");
+  TORCH_CHECK(pages.dim() == 1 && offsets.dim() == 1 && pages.size(0) == offsets.size(0) &&
+                  pages.size(0) == qkv.size(1),
+              "pages / offsets must be (T,) matching qkv");
+  TORCH_CHECK(pages.is_contiguous() && offsets.is_contiguous(), "pages / offsets contiguous");
+  check_i64(cu_seqlens, "cu_seqlens");
+  check_i64(kv_lens, "kv_lens");
+  check_i64(slot_ids, "slot_ids");
+  check_table(block_table);
+  const int64_t B = slot_ids.size(0);
+  TORCH_CHECK(kv_lens.dim() == 1 && kv_lens.size(0) == B, "kv_lens must be (B,)");
+  TORCH_CHECK(cu_seqlens.dim() == 1 && cu_seqlens.size(0) == B + 1, "cu_seqlens must be (B+1,)");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.size(1) == k_cache.size(0) &&
+                  block_table.stride(1) == 1,
+              "block_table must be (n_slots, n_pages) with contiguous rows");
+  TORCH_CHECK(cu_seqlens.is_contiguous() && kv_lens.is_contiguous() && slot_ids.is_contiguous(),
+              "cu_seqlens / kv_lens / slot_ids must be contiguous");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  at::Tensor o = rope_out(qkv, k_cache);
+  const int64_t T = qkv.size(1);
+  const int hq = static_cast<int>(o.size(2));
+  const int hkv = static_cast<int>(k_cache.size(1));
+  const size_t ws_bytes = cie_rope_kv_mixed_workspace_bytes(static_cast<int>(B), T, hq, hkv, 0,
+                                                            qkv.get_device());
+  at::Tensor ws = at::empty({static_cast<int64_t>((ws_bytes + 3) / sizeof(float))},
+                            qkv.options().dtype(at::kFloat));
+  const int st = with_table(
+      block_table,
+      [&](auto fn, auto* table) {
+        return fn(qkv.data_ptr(), qkv.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1),
+                  k_cache.data_ptr(), v_cache.data_ptr(), pages.data_ptr<int64_t>(),
+                  offsets.data_ptr<int64_t>(), max_seqlen, cu_seqlens.data_ptr<int64_t>(),
+                  kv_lens.data_ptr<int64_t>(), slot_ids.data_ptr<int64_t>(), table, o.data_ptr(),
+                  ws.data_ptr(), ws_bytes, static_cast<int>(B), T, hq, hkv,
+                  static_cast<int>(k_cache.size(3)), static_cast<int>(k_cache.size(2)),
+                  k_cache.size(0), block_table.size(0), block_table.stride(0),
+                  k_cache.stride(0), k_cache.stride(1), 0,
+                  reinterpret_cast<cie_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+      },
+      cie_rope_kv_mixed_attention, cie_rope_kv_mixed_attention_bt32);
+  check_status(st, "rope_kv_mixed_attention");
+  return o;
+}
+
 at::Tensor rope_kv_decode_attention(const at::Tensor& qkv, const at::Tensor& cos,
                                     const at::Tensor& sin, at::Tensor& k_cache,
                                     at::Tensor& v_cache, const at::Tensor& lens,
@@ -476,6 +532,10 @@ TORCH_LIBRARY(inference, m) {
       "rope_kv_mixed_update(Tensor qkv, Tensor cos, Tensor sin, Tensor(a!) k_cache, "
       "Tensor(b!) v_cache, Tensor pages, Tensor offsets) -> Tensor");
   m.def(
+      "rope_kv_mixed_attention(Tensor qkv, Tensor cos, Tensor sin, Tensor(a!) k_cache, "
+      "Tensor(b!) v_cache, Tensor pages, Tensor offsets, SymInt max_seqlen, Tensor cu_seqlens, "
+      "Tensor kv_lens, Tensor slot_ids, Tensor block_table) -> Tensor");
+  m.def(
       "rope_kv_decode_attention(Tensor qkv, Tensor cos, Tensor sin, Tensor(a!) k_cache, "
       "Tensor(b!) v_cache, Tensor lens, Tensor slot_ids, Tensor block_table) -> Tensor");
   m.def("rms_norm(Tensor x, Tensor weight, float eps) -> Tensor");
@@ -494,6 +554,7 @@ TORCH_LIBRARY_IMPL(inference, CUDA, m) {
   m.impl("rope_kv_decode_update", &rope_kv_decode_update);
   m.impl("rope_kv_mixed_update", &rope_kv_mixed_update);
   m.impl("rope_kv_decode_attention", &rope_kv_decode_attention);
+  m.impl("rope_kv_mixed_attention", &rope_kv_mixed_attention);
   m.impl("rms_norm", &rms_norm);
   m.impl("add_rms_norm", &add_rms_norm);
   m.impl("silu_and_mul", &silu_and_mul);

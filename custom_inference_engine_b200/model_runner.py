@@ -129,12 +129,17 @@ class PagedRunner:
 
     def __init__(self, model, max_cache_len: int, n_slots: int, page_seed: int = 0,
                  token_budget: int = 2048, fused_body: bool = True, mixed_graphs: bool = True,
-                 block_table_dtype=torch.int64, fused_lm_head: bool = True):
+                 block_table_dtype=torch.int64, fused_lm_head: bool = True,
+                 fused_mixed_attention: bool = True):
         from .attn.core import use_cuda_attention
         from .kv_cache.storage import KVStorage
 
         self.model = model
         use_cuda_attention(model)
+        # fused_mixed_attention: the metadata of this runner's mixed passes asks
+        # for RoPE, K/V write and attention as one call per layer (no piecewise
+        # splitter runs over this runner)
+        self.fused_mixed_attention = fused_mixed_attention
         self.device = next(model.parameters()).device
         self.dtype = next(model.parameters()).dtype
         self.kv = KVStorage(model.config, max_cache_len, PAGE_SIZE, n_slots, self.device,
@@ -215,6 +220,7 @@ class PagedRunner:
 
         positions, pages, offsets, cu = self.placement(slots, chunks)
         md = AttentionMetadata(token_count=int(cu[-1]), full_decode=False, device=self.device)
+        md.fuse_mixed_attention = self.fused_mixed_attention
         md.prepare_full_graph(len(slots))
         md.write_slot_ids(slots)
         md.write_cu_seqlens(cu)
@@ -380,6 +386,7 @@ class MixedGraph:
         self.max_seqs = max_seqs
         dev = runner.device
         self.md = AttentionMetadata(token_count=tokens, full_decode=False, device=dev)
+        self.md.fuse_mixed_attention = runner.fused_mixed_attention
         self.md.prepare_full_graph(max_seqs)
         z = lambda n: torch.zeros(n, dtype=torch.long, device=dev)
         self.ids, self.pos = z((1, tokens)), z((1, tokens))

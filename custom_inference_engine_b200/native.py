@@ -63,10 +63,17 @@ SIGNATURES = {
                                              c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_int,
                                              c_int, c_int, c_int, c_int, c_i64, c_i64, c_i64,
                                              c_i64, c_i64, c_int, c_ptr]),
+    "cie_rope_kv_mixed_workspace_bytes": (c_size, [c_int, c_i64, c_int, c_int, c_int, c_int]),
+    "cie_rope_kv_mixed_attention": (c_int, [c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr,
+                                            c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
+                                            c_ptr, c_ptr, c_size, c_int, c_i64, c_int, c_int,
+                                            c_int, c_int, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                            c_int, c_ptr]),
 }
 # the int32-block-table variants take the same arguments
 for _name in ("cie_decode_attention", "cie_mixed_attention", "cie_kv_decode_update",
-              "cie_rope_kv_decode_update", "cie_rope_kv_decode_attention"):
+              "cie_rope_kv_decode_update", "cie_rope_kv_decode_attention",
+              "cie_rope_kv_mixed_attention"):
     SIGNATURES[_name + "_bt32"] = SIGNATURES[_name]
 SIGNATURES.update({
     # include/cie_model_ops.h
@@ -174,6 +181,11 @@ def _register_fakes() -> None:
 
     @torch.library.register_fake("inference::rope_kv_mixed_update")
     def _rope_mix_fake(qkv, cos, sin, k_cache, v_cache, pages, offsets):
+        return _rope_out(qkv, k_cache)
+
+    @torch.library.register_fake("inference::rope_kv_mixed_attention")
+    def _rope_mix_attn_fake(qkv, cos, sin, k_cache, v_cache, pages, offsets, max_seqlen,
+                            cu_seqlens, kv_lens, slot_ids, block_table):
         return _rope_out(qkv, k_cache)
 
     @torch.library.register_fake("inference::rope_kv_decode_attention")

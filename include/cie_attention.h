@@ -259,6 +259,39 @@ int cie_rope_kv_decode_attention(const void* qkv, int64_t qkv_tok_stride, const 
                                  int64_t n_slots, int64_t bt_stride, int64_t cache_page_stride,
                                  int64_t cache_head_stride, int num_splits, cie_stream_t stream);
 
+/* ---- rotary embedding + KV write + mixed attention in one call -------------- */
+
+/*
+ * The whole attention step of a mixed pass (chunked prefill + decode rows):
+ * the rotary embedding of q and k from the fused QKV projection, the write of
+ * every token's k and v row to (pages[t], offsets[t]) -- what
+ * cie_rope_kv_mixed_update does -- and cie_mixed_attention over the pass, with
+ * no second call. Replaces attn/core.py:193-206 + :217-233 of the reference
+ * (apply_rotary_pos_emb, KVStorage.mixed_update, the mixed attention op). The
+ * planning kernel of the attention runs in the same grid as the rotation and
+ * the K/V write (extra CTAs), and the attention kernel starts after that grid,
+ * so it reads the pages as written. pages / offsets must address the rows that
+ * block_table gives the same positions (the reference's AttentionMetadata does).
+ * Output and pages are bit-identical to cie_rope_kv_mixed_update followed by
+ * cie_mixed_attention. Arguments: those of the two calls; the rotated q lives in
+ * the workspace (cie_rope_kv_mixed_workspace_bytes bytes, 16-byte aligned, no
+ * initialisation).
+ */
+size_t cie_rope_kv_mixed_workspace_bytes(int batch, int64_t total_tokens, int num_q_heads,
+                                         int num_kv_heads, int num_splits, int device);
+
+int cie_rope_kv_mixed_attention(const void* qkv, int64_t qkv_tok_stride, const void* cos,
+                                const void* sin, int64_t cs_tok_stride, void* k_cache,
+                                void* v_cache, const int64_t* pages, const int64_t* offsets,
+                                int64_t max_seqlen, const int64_t* cu_seqlens,
+                                const int64_t* kv_lens, const int64_t* slot_ids,
+                                const int64_t* block_table, void* o, void* workspace,
+                                size_t workspace_bytes, int batch, int64_t total_tokens,
+                                int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+                                int64_t cache_page_stride, int64_t cache_head_stride,
+                                int num_splits, cie_stream_t stream);
+
 /* ---- int32 block table ------------------------------------------------------
  * The reference keeps the block table as int64 (kv_cache/storage.py:52-56) and
  * every entry point above takes it so. These variants take the same table as
@@ -308,6 +341,15 @@ int cie_rope_kv_decode_attention_bt32(
     size_t workspace_bytes, int batch, int num_q_heads, int num_kv_heads, int head_dim,
     int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride, int64_t cache_page_stride,
     int64_t cache_head_stride, int num_splits, cie_stream_t stream);
+
+int cie_rope_kv_mixed_attention_bt32(
+    const void* qkv, int64_t qkv_tok_stride, const void* cos, const void* sin,
+    int64_t cs_tok_stride, void* k_cache, void* v_cache, const int64_t* pages,
+    const int64_t* offsets, int64_t max_seqlen, const int64_t* cu_seqlens, const int64_t* kv_lens,
+    const int64_t* slot_ids, const int32_t* block_table, void* o, void* workspace,
+    size_t workspace_bytes, int batch, int64_t total_tokens, int num_q_heads, int num_kv_heads,
+    int head_dim, int page_size, int64_t n_pages, int64_t n_slots, int64_t bt_stride,
+    int64_t cache_page_stride, int64_t cache_head_stride, int num_splits, cie_stream_t stream);
 
 #ifdef __cplusplus
 }

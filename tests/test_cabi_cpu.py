@@ -207,3 +207,25 @@ def test_bt32_variants_check_arguments_like_the_int64_ones():
     assert lib.cie_decode_attention_bt32(*args, 4, None) == -5   # split path without workspace
     assert lib.cie_kv_decode_update_bt32(p, p, p, p, None, p, p, 4, 2, 64, 16, 10, 3, 10, 2048,
                                          1024, 1152, 64, 1152, 64, None) == -1
+
+
+def test_rope_kv_mixed_attention_argument_checks():
+    """The one-call RoPE + K/V write + mixed attention rejects bad arguments
+    on the host: missing pages, a workspace without room for the rotated q."""
+    lib = native.lib()
+    p = 1 << 20
+
+    def call(**kw):
+        a = dict(qkv=p, qkv_tok=1152, cos=p, sin=p, cs_tok=64, k=p, v=p, pages=p, offsets=p,
+                 max_seqlen=16, cu=p, kvl=p, slots=p, bt=p, o=p, ws=p, ws_bytes=0, batch=2,
+                 T=16, hq=14, hkv=2, d=64, page=16, n_pages=10, n_slots=3, bt_stride=10,
+                 pstride=2048, hstride=1024, splits=0, stream=None)
+        a.update(kw)
+        return lib.cie_rope_kv_mixed_attention(*a.values())
+    assert call(pages=None) == -1
+    assert call(d=128) == -2
+    need = lib.cie_rope_kv_mixed_workspace_bytes(2, 16, 14, 2, 0, -1)
+    assert need >= lib.cie_mixed_workspace_bytes(2, 16, 2, 0, -1) + 16 * 14 * 64 * 2
+    assert call(ws_bytes=need - 1) == -5
+    assert call(qkv_tok=1000, ws_bytes=need) == -1      # qkv rows overlap
+    assert call(batch=0, T=0) == 0
