@@ -79,6 +79,19 @@ def main() -> int:
         del c
         torch.cuda.empty_cache()
 
+    if args.points == "sweep":
+        # config 1: B = 8, kv_lens ~ U[1, 2048] from torch.Generator seed 0
+        c = W.make_decode_case(W.config1_lens(), seed=0, device=dev, generate_on_device=True)
+
+        def fn():
+            dec_op(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table)
+        for _ in range(3):
+            fn()
+        ms = bench.graph_time_cold(fn, dev)
+        out["config1"] = {"us_per_call": ms * 1e3,
+                          "gbs": c.algorithmic_bytes() / (ms / 1e3) / 1e9}
+        del c
+
     g = torch.Generator().manual_seed(1)
     kv512 = torch.randint(0, 8193, (4,), generator=g).tolist()
     chunk3, kv3 = W.config3_shape(seed=0)

@@ -569,17 +569,56 @@ def reference_triton_times(points: str = "sweep"):
     return json.loads(run.stdout.strip().splitlines()[-1])
 
 
-def sweep_with_reference(dev):
+def config1_point(dev, cpu: bool = True):
+    """Config 1 itself: B = 8 sequences, kv_lens ~ U[1, 2048] (torch.Generator
+    seed 0), one decode call timed with a cold L2, and the fp32 CPU oracle on
+    the same call (all host cores)."""
+    from custom_inference_engine_b200 import workloads as W
+    from custom_inference_engine_b200.attn import core
+    lens = W.config1_lens()
+    c = W.make_decode_case(lens, seed=0, device=dev, generate_on_device=True)
+
+    def fn():
+        core.gqa_decode_attention_op(c.q, c.k, c.v, c.lens, slot_ids=c.slot_ids,
+                                     block_table=c.block_table)
+    for _ in range(3):
+        fn()
+    ms = graph_time_cold(fn, dev)
+    nbytes = c.algorithmic_bytes()
+    peak, _ = measured_peak_gbs()
+    out = {"sweep": "config1", "batch": len(lens), "kv_lens": lens, "us_per_call": ms * 1e3,
+           "gbs": nbytes / (ms / 1e3) / 1e9, "frac_of_measured_hbm": nbytes / (ms / 1e3) / 1e9 / peak,
+           "algorithmic_bytes": nbytes}
+    if cpu:
+        import oracle
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        h = [t.cpu() for t in (c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table)]
+        oracle.decode_attention_fp32(*h)
+        t0, n = time.perf_counter(), 0
+        while time.perf_counter() - t0 < 3.0:
+            oracle.decode_attention_fp32(*h)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        out["cpu_baseline"] = {"value": nbytes / dt / 1e9, "unit": UNIT, "cores": threads,
+                               "kind": "port", "sample": f"{n} calls, {dt * 1e3:.2f} ms each"}
+    return out
+
+
+def sweep_with_reference(dev, cpu: bool = True):
     """Our sweep points side by side with the reference Triton kernels' times
     for the points both measure (same workloads, same timing method)."""
-    ours = sweep_points(dev)
+    ours = [config1_point(dev, cpu)] + sweep_points(dev)
     ref = reference_triton_times("sweep")
     by_point = {}
     for r in ref.get("decode", []):
         by_point[(r["batch"], r["kv_len"], r["num_programs"])] = r
     for p in ours:
-        key = (p["batch"], p["kv_len"], p["num_splits"] if p["sweep"] == "config5" else 16)
-        r = by_point.get(key)
+        if p["sweep"] == "config1":
+            r = ref.get("config1")
+        else:
+            key = (p["batch"], p["kv_len"], p["num_splits"] if p["sweep"] == "config5" else 16)
+            r = by_point.get(key)
         if r is not None:
             p["reference_triton_us"] = r["us_per_call"]
             p["speedup_vs_reference_triton"] = r["us_per_call"] / p["us_per_call"]
@@ -984,7 +1023,7 @@ def run_ours(args, rank, world, local):
         if not args.no_mixed:
             result["mixed"] = mixed_lines(dev, cpu=world == 1 and not args.no_cpu_baseline)
         if world == 1 and not args.no_sweep:
-            result["sweep"], ref = sweep_with_reference(dev)
+            result["sweep"], ref = sweep_with_reference(dev, cpu=not args.no_cpu_baseline)
             result["reference_triton"] = ref
             result["lm_head"] = lm_head_line(dev)
         if not args.no_cpu_baseline and world == 1:

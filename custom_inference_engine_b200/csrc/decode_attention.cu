@@ -720,10 +720,12 @@ int cie_decode_default_splits(int batch, int device) {
       sms = n;
   }
   if (batch <= 0) return 1;
-  // two resident CTAs per SM; one wave of (split, sequence) CTAs
+  // two resident CTAs per SM; one wave of (split, sequence) CTAs, at most 64
+  // splits: past that the merge of the partials costs more than the extra
+  // parallelism gives (B = 1 x 16384: 12.1 us at 64 splits, 16.0 us at 256)
   int s = (2 * sms) / batch;
   if (s < 1) s = 1;
-  if (s > 256) s = 256;
+  if (s > 64) s = 64;
   return s;
 }
 

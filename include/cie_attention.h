@@ -69,7 +69,8 @@ int cie_read_device_errors(int device, unsigned int* bits, int clear);
 /* ---- split-KV paged GQA decode ------------------------------------------- */
 
 /* Split count used when cie_decode_attention() is given num_splits <= 0:
- * enough (sequence, split) CTAs to keep every SM of `device` streaming. */
+ * enough (sequence, split) CTAs to keep every SM of `device` streaming
+ * (two per SM), at most 64. */
 int cie_decode_default_splits(int batch, int device);
 
 /* Bytes of fp32 workspace the split path needs (0 when num_splits == 1). */

@@ -43,6 +43,7 @@ def test_host_only_queries():
     assert lib.cie_decode_default_splits(0, -1) == 1
     assert lib.cie_decode_default_splits(256, -1) == 1
     assert lib.cie_decode_default_splits(8, -1) == 37
+    assert lib.cie_decode_default_splits(1, -1) == 64   # capped: the merge outgrows the gain
 
 
 def _decode(**kw):
