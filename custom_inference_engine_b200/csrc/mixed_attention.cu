@@ -107,10 +107,15 @@ constexpr uint32_t kColO = 192;
 constexpr uint32_t kIdescS = idesc_f16_f32(kM, kBlockKeys, false);
 constexpr uint32_t kIdescPV = idesc_f16_f32(kM, kD, true);
 
-// partial record of one row: unnormalised O[64], m (log2 units: max of score
-// * scale * log2(e)), l
-constexpr int kPartFloats = kD + 2;
-constexpr int kRecRows = 2 * kRows;  // one record = the rows of both tiles of a pair
+// Partial record of one piece of a tile pair: per row, the unnormalised O[64],
+// m (log2 units: max of score * scale * log2(e)) and l, stored column-major as
+// [kPartCols][kRecRows] float2 -- column cc < kD / 2 holds (O[2cc], O[2cc+1]),
+// column kD / 2 holds (m, l). Tile x's row r sits at x * kM + r, so a warp's
+// 32 rows of one column are 256 contiguous, aligned bytes for both the
+// writing and the merging CTA.
+constexpr int kPartCols = kD / 2 + 1;
+constexpr int kPartFloats = 2 * kPartCols;
+constexpr int kRecRows = 2 * kM;
 
 // The work plan, in the caller's workspace. A work item is one CTA: a tile
 // pair of one (sequence, kv head) and a contiguous range of its key blocks.
@@ -122,7 +127,7 @@ struct Plan {
   int* header;         // [0] items
   int4* items;
   unsigned* counters;  // per split pair: pieces finished
-  float* records;      // [record][kRecRows][kPartFloats]
+  float* records;      // [record][kPartCols][kRecRows] float2
   int max_items, max_split, max_rec;
 };
 
@@ -482,23 +487,25 @@ __global__ void __launch_bounds__(kPlanThreads)
 // record, this CTA's included, is written before the last piece gets here):
 // O = sum_q w_q acc_q / sum_q w_q l_q with w_q = 2^(m_q - max m), m in log2
 // units. Out of line, so that its registers do not weigh on the softmax loop.
-__device__ __noinline__ void merge_row(const float* rec0, int n_pieces, __half* dst) {
-  constexpr int64_t kStride = static_cast<int64_t>(kRecRows) * kPartFloats;
+// `rec0` points at the row's (O[0], O[1]) entry of the pair's first record.
+__device__ __noinline__ void merge_row(const float2* rec0, int n_pieces, __half* dst) {
+  constexpr int64_t kStride = static_cast<int64_t>(kRecRows) * kPartCols;
+  constexpr int kML = (kD / 2) * kRecRows;
   float M = -CUDART_INF_F;
-  for (int q = 0; q < n_pieces; ++q) M = fmaxf(M, __ldcg(rec0 + q * kStride + kD));
+  for (int q = 0; q < n_pieces; ++q) M = fmaxf(M, __ldcg(rec0 + q * kStride + kML).x);
   float acc[kD];
 #pragma unroll
   for (int d = 0; d < kD; ++d) acc[d] = 0.f;
   float den = 0.f;
   for (int q = 0; q < n_pieces; ++q) {
-    const float* rec = rec0 + q * kStride;
-    const float mq = __ldcg(rec + kD);
-    if (mq == -CUDART_INF_F) continue;  // no visible key in this piece's range
-    const float w = ex2(mq - M);
-    den += w * __ldcg(rec + kD + 1);
+    const float2* rec = rec0 + q * kStride;
+    const float2 ml = __ldcg(rec + kML);
+    if (ml.x == -CUDART_INF_F) continue;  // no visible key in this piece's range
+    const float w = ex2(ml.x - M);
+    den += w * ml.y;
 #pragma unroll
     for (int cc = 0; cc < kD / 2; ++cc) {
-      const float2 a = __ldcg(reinterpret_cast<const float2*>(rec) + cc);
+      const float2 a = __ldcg(rec + cc * kRecRows);
       acc[2 * cc] += w * a.x;
       acc[2 * cc + 1] += w * a.y;
     }
@@ -885,17 +892,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                      : "l"(p.plan.items + 2 * blockIdx.x + 1));
         const int rec0 = im.x, split = im.y, piece = im.z, n_pieces = im.w;
         if (row_valid) {
-          float* rec = p.plan.records +
-                       (static_cast<int64_t>(rec0 + piece) * kRecRows + x * kRows + row) * kPartFloats;
+          float2* rec = reinterpret_cast<float2*>(p.plan.records) +
+                        static_cast<int64_t>(rec0 + piece) * kRecRows * kPartCols + x * kM + row;
 #pragma unroll
           for (int cc = 0; cc < kD / 2; ++cc)
-            reinterpret_cast<float2*>(rec)[cc] =
+            rec[cc * kRecRows] =
                 make_float2(__uint_as_float(ob[cc * 2 + 0]), __uint_as_float(ob[cc * 2 + 1]));
           // a piece whose pipeline wait gave up (ok == false; the device
           // error bit is set) publishes an empty range, which the merge skips,
           // instead of whatever its accumulators hold
-          rec[kD] = ok ? m_ref : -CUDART_INF_F;
-          rec[kD + 1] = ok ? l_run : 0.f;
+          rec[(kD / 2) * kRecRows] =
+              ok ? make_float2(m_ref, l_run) : make_float2(-CUDART_INF_F, 0.f);
         }
         __threadfence();
         // every working softmax thread of both tiles has published its rows
@@ -909,8 +916,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("bar.sync 1, %0;" ::"r"(n_thr) : "memory");
         if (*last_flag != 0 && row_valid && ok) {
           __threadfence();
-          merge_row(p.plan.records + (static_cast<int64_t>(rec0) * kRecRows + x * kRows + row) *
-                                         kPartFloats,
+          merge_row(reinterpret_cast<const float2*>(p.plan.records) +
+                        static_cast<int64_t>(rec0) * kRecRows * kPartCols + x * kM + row,
                     n_pieces, p.o + (tok * p.num_q_heads + hq) * kD);
         }
       }

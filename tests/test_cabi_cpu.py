@@ -95,7 +95,7 @@ def test_mixed_and_update_argument_checks():
     assert mixed(batch=2049, T=4096, max_seqlen=16) == -2
 
     def plan_bytes(batch, T, hkv, splits, sms=148):
-        # header | items (2 x int4) | split counters | records of 252 rows x 66 fp32
+        # header | items (2 x int4) | split counters | records of 2 x 128 rows x 66 fp32
         r256 = lambda x: (x + 255) // 256 * 256
         units = hkv * ((T + 35) // 36 + batch)
         if splits >= 1:
@@ -103,7 +103,7 @@ def test_mixed_and_update_argument_checks():
                 (splits * units if splits > 1 else 0)
         else:
             items, split, rec = units + sms, sms, 2 * sms
-        return 256 + r256(items * 32) + r256(split * 4) + rec * 252 * 66 * 4
+        return 256 + r256(items * 32) + r256(split * 4) + rec * 256 * 66 * 4
     for args in ((4, 2048, 2, 1), (4, 2048, 2, 3), (4, 2048, 2, 0), (32, 2048, 2, 0),
                  (1, 1, 2, 16)):
         assert lib.cie_mixed_workspace_bytes(*args, -1) == plan_bytes(*args)
