@@ -504,13 +504,14 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
 // merge, kernels/decode_attention.py:243-264). 8 warps each fold every 8th
 // split (lane = two output columns), then warp 0 folds the 8 warp results.
 // Launched with programmatic stream serialization: griddepcontrol.wait holds
-// it until the split kernel has finished and its writes are visible.
+// it until the split kernel has finished and its writes are visible (the
+// sequence's page count, from inputs the split kernel does not write, is read
+// before).
 __global__ void __launch_bounds__(256)
     decode_merge_kernel(const float* __restrict__ ws_acc, const float* __restrict__ ws_ml,
                         __half* __restrict__ o, const int64_t* __restrict__ lens,
                         const int64_t* __restrict__ slot_ids, int64_t n_slots,
                         int64_t bt_stride, int num_splits, int num_q_heads, int lens_per_slot) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float s_m[8], s_l[8];
   __shared__ float2 s_acc[8][32];
   const int hq = blockIdx.x;
@@ -518,7 +519,9 @@ __global__ void __launch_bounds__(256)
   const int S = num_splits;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // the split kernel does not write lengths or slots: read them while it runs
   const int np = seq_pages(lens, slot_ids, b, n_slots, bt_stride, lens_per_slot);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int pps = split_pages(np, S);
   const int active = np == 0 ? 0 : (np + pps - 1) / pps;
 
@@ -579,12 +582,13 @@ __global__ void __launch_bounds__(1024)
                               const int64_t* __restrict__ slot_ids, int64_t n_slots,
                               int64_t bt_stride, int num_splits, int num_q_heads,
                               int lens_per_slot) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int hq = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x;
   const int S = num_splits;
+  // the split kernel does not write lengths or slots: read them while it runs
   const int np = seq_pages(lens, slot_ids, b, n_slots, bt_stride, lens_per_slot);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int pps = split_pages(np, S);
   const int active = np == 0 ? 0 : (np + pps - 1) / pps;
 
