@@ -162,6 +162,20 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
   const int b = blockIdx.y;
   const int S = p.num_splits;
 
+  // Launched as a programmatic dependent of the previous kernel in the stream:
+  // the barriers and the tensor-map prefetch need none of its results, every
+  // read of an input comes after griddepcontrol.wait.
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, HKV);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
   // ---- per-sequence page range of this split -------------------------------
   int64_t slot = p.slot_ids[b];
   bool bad = false;
@@ -185,11 +199,6 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
   const int Li = static_cast<int>(L);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(full0 + 8u * s, 1);
-      mbar_init(empty0 + 8u * s, HKV);
-    }
-    fence_mbar_init();
     // let the merge kernel (launched with programmatic stream serialization)
     // get scheduled while this grid streams; it waits for our completion
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -198,10 +207,6 @@ __global__ void __launch_bounds__(Cfg<HKV>::kThreads)
 
   if (warp == 0) {
     // ======================= producer warp ==================================
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-    }
     const int64_t bt_row = slot * p.bt_stride + page_begin;
     auto page_id = [&](int j) -> int {  // block-table entry j of this split, checked
       if (j >= n) return 0;
@@ -686,9 +691,19 @@ int launch(const void* q, const void* k, const void* v, const int64_t* lens,
     p.k_cache = static_cast<__half*>(const_cast<void*>(k));
     p.v_cache = static_cast<__half*>(const_cast<void*>(v));
   }
-  dim3 grid(S, batch);
-  decode_split_kernel<HKV><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tm_k, tm_v, p);
-  cudaError_t e = cudaGetLastError();
+  // a programmatic dependent of the previous kernel in the stream: scheduled
+  // as that kernel drains, it waits (griddepcontrol.wait) before reading inputs
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t scfg = {};
+  scfg.gridDim = dim3(S, batch);
+  scfg.blockDim = dim3(C::kThreads);
+  scfg.dynamicSmemBytes = C::kSmemBytes;
+  scfg.stream = stream;
+  scfg.attrs = pdl;
+  scfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&scfg, decode_split_kernel<HKV>, tm_k, tm_v, p);
   if (e != cudaSuccess) return fail(CIE_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
   if (S > 1) {
     const bool small = S <= kSmallMergeSplits;
