@@ -87,6 +87,10 @@ size_t cie_decode_workspace_bytes(int batch, int num_q_heads, int head_dim, int 
  * num_splits: KV splits per sequence (<= 0: cie_decode_default_splits).
  * workspace: >= cie_decode_workspace_bytes(...) bytes, 16-byte aligned
  * (may be NULL when the split count resolves to 1).
+ * Launches the split kernel as a programmatic dependent of the preceding
+ * kernel in `stream` (no input is read before its griddepcontrol.wait, so a
+ * producer kernel that triggers early is safe) and, with more than one split,
+ * the merge kernel as a programmatic dependent of the split kernel.
  */
 int cie_decode_attention(const void* q, const void* k, const void* v, const int64_t* lens,
                          const int64_t* slot_ids, const int64_t* block_table, void* o,
