@@ -88,6 +88,21 @@ def test_config2_points_against_fp32(B, L, cuda_device):
     assert _maxabs(o, ref) <= TOL
 
 
+def test_very_long_and_tiny_sequences_together(cuda_device):
+    # one 262 144-key context (16 384 pages: 256 per split at the default 64
+    # splits for B = 3) beside a 1-key and a 17-key sequence: most of the short
+    # rows' splits have no page
+    c = W.make_decode_case([262144, 1, 17], seed=9, device=cuda_device, generate_on_device=True)
+    ref = torch.cat([torch_decode_fp32(c.q[:, b:b + 1], c.k, c.v, c.lens[b:b + 1],
+                                       c.slot_ids[b:b + 1], c.block_table)
+                     for b in range(3)], dim=1)
+    for splits in (0, 1, 64):
+        o = cabi.decode_attention(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table,
+                                  num_splits=splits)
+        assert torch.isfinite(o.float()).all()
+        assert _maxabs(o, ref) <= TOL
+
+
 @pytest.mark.parametrize("splits", [4, 8, 16, 32, 64])
 def test_long_context_split_sweep(splits, cuda_device):
     # config 5 shape per GPU: 8 sequences x 32768 keys, pages scattered

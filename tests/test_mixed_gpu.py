@@ -92,6 +92,8 @@ def test_golden_cases_cabi(name, splits, cuda_device):
     ([18, 19, 36, 37], [0, 5, 128, 129]),    # query-tile edges
     ([128, 129, 255], [127, 0, 1]),          # key-block edges
     ([300], [4000]),
+    ([36, 5], [60000, 30000]),               # pairs cut into the most pieces (merge of 16)
+    ([2048], [0]),                           # one long prompt: every tile pair of a sequence
 ])
 def test_edge_shapes(chunks, kvs, cuda_device):
     c = W.make_mixed_case(chunks, kvs, seed=sum(chunks) + sum(kvs))
