@@ -178,40 +178,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ============================ MMA issuer ==================================
-    if (lane == 0) {
-      bool ok = mbar_wait(bars.h_full(), 0, CIE_DEVERR_WAIT_TIMEOUT);
-      int consumed = 0;
-      for (int i = 0; i < my_chunks && ok; ++i) {
-        const int buf = i & 1;
-        if (i >= 2 && !mbar_wait(bars.acc_empty(buf), static_cast<uint32_t>((i >> 1) - 1) & 1u,
-                                 CIE_DEVERR_WAIT_TIMEOUT)) {
+    // The whole warp runs the loop; one elected lane issues each MMA and commit
+    // (a single-lane branch issues slowly beside a busy epilogue warp).
+    bool ok = __all_sync(0xffffffffu, mbar_wait(bars.h_full(), 0, CIE_DEVERR_WAIT_TIMEOUT));
+    int consumed = 0;
+    for (int i = 0; i < my_chunks && ok; ++i) {
+      const int buf = i & 1;
+      if (i >= 2 &&
+          !__all_sync(0xffffffffu, mbar_wait(bars.acc_empty(buf),
+                                             static_cast<uint32_t>((i >> 1) - 1) & 1u,
+                                             CIE_DEVERR_WAIT_TIMEOUT))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + static_cast<uint32_t>(buf * kMaxN);
+      for (int kb = 0; kb < p.k_blocks; ++kb, ++consumed) {
+        const int s = consumed % kStages;
+        if (!__all_sync(0xffffffffu, mbar_wait(bars.full(s),
+                                               static_cast<uint32_t>(consumed / kStages) & 1u,
+                                               CIE_DEVERR_WAIT_TIMEOUT))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(buf * kMaxN);
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++consumed) {
-          const int s = consumed % kStages;
-          if (!mbar_wait(bars.full(s), static_cast<uint32_t>(consumed / kStages) & 1u,
-                         CIE_DEVERR_WAIT_TIMEOUT)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
 #pragma unroll
-          for (int k = 0; k < kKBlock / 16; ++k) {
-            const uint64_t da = smem_desc(sRing + s * kWBoxBytes + k * 32, 16, 1024);
-            const uint64_t db = smem_desc(sH + kb * kHBlockBytes + k * 32, 16, 1024);
-            tc_mma_f16(d, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          }
-          tc_commit(bars.empty(s));
+        for (int k = 0; k < kKBlock / 16; ++k) {
+          const uint64_t da = smem_desc(sRing + s * kWBoxBytes + k * 32, 16, 1024);
+          const uint64_t db = smem_desc(sH + kb * kHBlockBytes + k * 32, 16, 1024);
+          tc_mma_f16_elect(d, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
         }
-        if (ok) tc_commit(bars.acc_full(buf));
+        tc_commit_elect(bars.empty(s));
       }
-      // every MMA issued here has completed before TMEM is freed
-      tc_commit(bars.done());
-      mbar_wait(bars.done(), 0, CIE_DEVERR_WAIT_TIMEOUT);
+      if (ok) tc_commit_elect(bars.acc_full(buf));
     }
+    // every MMA issued here has completed before TMEM is freed
+    tc_commit_elect(bars.done());
+    mbar_wait(bars.done(), 0, CIE_DEVERR_WAIT_TIMEOUT);
     __syncwarp();
   } else if (warp >= 4) {
     // ============================ epilogue ====================================

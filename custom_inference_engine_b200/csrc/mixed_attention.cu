@@ -661,15 +661,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else if (warp <= 2) {
       // ======================= MMA issuers (warp 1: tile A, warp 2: tile B) ===
-      // One thread per tile, in order: S(j) = Q K_j^T as soon as K_j is in and
+      // One warp per tile, in order: S(j) = Q K_j^T as soon as K_j is in and
       // the softmax has read S(j-1), then O += P(j-1) V_{j-1} once P(j-1) is
       // published. A tile's QK^T is never queued behind the other tile's P.V
       // issue, and S(j) goes ahead of PV(j-1), which the softmax needs later.
+      // The whole warp runs the loop and one elected lane issues each MMA and
+      // commit (the warp shares its SM sub-partition with two softmax warps,
+      // which would starve a single-lane issuing branch).
       const int x = warp - 1;
-      if (lane == 0 && x < n_tiles) {
-        bool ok = mbar_wait(bars.q_full(), 0, CIE_DEVERR_WAIT_TIMEOUT);
+      if (x < n_tiles) {
+        bool ok = __all_sync(0xffffffffu, mbar_wait(bars.q_full(), 0, CIE_DEVERR_WAIT_TIMEOUT));
         auto wait = [&](uint32_t bar, uint32_t parity) {
-          if (ok && !mbar_wait(bar, parity, CIE_DEVERR_WAIT_TIMEOUT)) ok = false;
+          if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar, parity, CIE_DEVERR_WAIT_TIMEOUT));
           return ok;
         };
         auto issue_pv = [&](int j) {  // O_x (+)= P_x(j) V_j, P from TMEM
@@ -680,11 +683,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kBlockKeys / 16; ++kk) {
             // 16 keys = 8 P columns; V: 16 keys = two 8-row swizzle atoms of 1 KiB
             const uint64_t db = smem_desc(v_tile + kk * 2048, kKVTileBytes, 1024);
-            tc_mma_f16_ts(tmem + x * 256 + kColO, tmem + x * 256 + kColP + kk * 8, db, kIdescPV,
-                          (j > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_f16_ts_elect(tmem + x * 256 + kColO, tmem + x * 256 + kColP + kk * 8, db,
+                                kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(bars.pv_done(x));
-          tc_commit(bars.kv_empty(j % kStages));  // this tile is done with K_j and V_j
+          tc_commit_elect(bars.pv_done(x));
+          tc_commit_elect(bars.kv_empty(j % kStages));  // this tile is done with K_j and V_j
         };
         for (int j = 0; j < n_blocks && ok; ++j) {
           if (!wait(bars.kv_full(j % kStages), static_cast<uint32_t>(j / kStages) & 1u)) break;
@@ -695,14 +698,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < kD / 16; ++k) {  // S_x(j) = Q_x K_j^T
             const uint64_t da = smem_desc(sQ + x * kQBytes + k * 32, 16, 1024);
             const uint64_t db = smem_desc(k_tile + k * 32, 16, 1024);
-            tc_mma_f16(tmem + x * 256 + kColS, da, db, kIdescS, k > 0 ? 1u : 0u);
+            tc_mma_f16_elect(tmem + x * 256 + kColS, da, db, kIdescS, k > 0 ? 1u : 0u);
           }
-          tc_commit(bars.s_full(x));
+          tc_commit_elect(bars.s_full(x));
           if (j > 0) issue_pv(j - 1);
         }
         if (ok && n_blocks > 0) issue_pv(n_blocks - 1);
-        // drain: every MMA this thread issued has completed before TMEM is freed
-        tc_commit(bars.mma_done(x));
+        // drain: every MMA this warp issued has completed before TMEM is freed
+        tc_commit_elect(bars.mma_done(x));
         mbar_wait(bars.mma_done(x), 0, CIE_DEVERR_WAIT_TIMEOUT);
       }
       __syncwarp();

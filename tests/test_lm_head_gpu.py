@@ -14,6 +14,8 @@ import torch
 from custom_inference_engine_b200 import cabi, native
 from custom_inference_engine_b200 import model_runner as MR
 
+native.load_ops()  # torch.ops.inference.* (also when this file runs alone)
+
 pytestmark = pytest.mark.gpu
 VOCAB, HIDDEN = 151936, 896
 
