@@ -73,6 +73,32 @@ def test_other_shapes(vocab, hidden, cuda_device):
     _check(h, w)
 
 
+def test_maximum_at_every_range_edge(cuda_device):
+    """The maximum placed on 128-row chunk edges, on the vocab's last rows and on
+    the first and last rows of every range of an even split into 148 or 132
+    parts is found (each position in its own hidden row)."""
+    hidden = 64
+    g = torch.Generator(device=cuda_device).manual_seed(11)
+    w = (torch.randn(VOCAB, hidden, generator=g, device=cuda_device) * 0.02).half()
+    units = (VOCAB + 15) // 16
+    pos = {0, 127, 128, 1023, 1024, 1039, 1040, VOCAB - 17, VOCAB - 16, VOCAB - 1}
+    for grid in (148, 132):
+        for c in range(grid):
+            pos.add(units * c // grid * 16)
+            pos.add(min(units * (c + 1) // grid * 16, VOCAB) - 1)
+    pos = sorted(pos)
+    eye = torch.eye(hidden, dtype=torch.float16, device=cuda_device)
+    for i0 in range(0, len(pos), hidden):
+        rows = pos[i0:i0 + hidden]
+        w2 = w.clone()
+        for i, r in enumerate(rows):
+            w2[r] = 4 * eye[i]      # logit 4 for h row i, about 0.02 everywhere else
+        h = eye[:len(rows)].contiguous()
+        tokens, logits = cabi.lm_head_argmax(h, w2, logits=True)
+        assert torch.equal(tokens, logits.argmax(dim=-1))
+        assert tokens.tolist() == rows
+
+
 def test_ties_nan_and_zero_rows(cuda_device):
     g = torch.Generator(device=cuda_device).manual_seed(3)
     w = (torch.randn(4096, HIDDEN, generator=g, device=cuda_device) * 0.02).half()
