@@ -74,13 +74,14 @@ def test_config1_full(cuda_device):
         assert _maxabs(o, g["out"]) <= TOL
 
 
-@pytest.mark.parametrize("B,L", [(1, 512), (2, 16384), (8, 4096), (32, 512), (64, 4096),
-                                 (128, 512), (256, 4096), (256, 16384)])
+@pytest.mark.parametrize("L", [512, 4096, 16384])
+@pytest.mark.parametrize("B", [1, 2, 4, 8, 16, 32, 64, 128, 256])
 def test_config2_points_against_fp32(B, L, cuda_device):
-    # (256, 16384) is the largest config-2 pool: 262 145 pages, 2 GiB per K or
-    # V, K/V offsets up to 5.4e8 elements and 4.2 M block-table entries, the
-    # size where the reference's int32 offset guards (attn/core.py:24-34)
-    # start to matter; this build addresses the pools with 64-bit offsets
+    # every point of the config-2 grid at the default split count; (256, 16384)
+    # is the largest pool: 262 145 pages, 2 GiB per K or V, K/V offsets up to
+    # 5.4e8 elements and 4.2 M block-table entries, the size where the
+    # reference's int32 offset guards (attn/core.py:24-34) start to matter;
+    # this build addresses the pools with 64-bit offsets
     c = W.make_decode_case([L] * B, seed=7, device=cuda_device, generate_on_device=True)
     ref = torch_decode_fp32(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table)
     o = cabi.decode_attention(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table)
@@ -101,6 +102,31 @@ def test_very_long_and_tiny_sequences_together(cuda_device):
                                   num_splits=splits)
         assert torch.isfinite(o.float()).all()
         assert _maxabs(o, ref) <= TOL
+
+
+@pytest.mark.parametrize("B,seed", [(3, 1), (37, 2), (200, 3)])
+def test_ragged_batches(B, seed, cuda_device):
+    # lengths drawn from 0 .. 9000 (zeros included) in one batch, default and
+    # explicit split counts; zero-length rows must come out exactly zero
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(0, 9001, (B,), generator=g)
+    lens[::7] = 0
+    lens = lens.tolist()
+    c = W.make_decode_case(lens, seed=seed, device=cuda_device, generate_on_device=True)
+    parts = []
+    for b, L in enumerate(lens):
+        if L == 0:
+            parts.append(torch.zeros(1, 1, 14, 64, dtype=torch.float16, device=cuda_device))
+        else:
+            parts.append(torch_decode_fp32(c.q[:, b:b + 1], c.k, c.v, c.lens[b:b + 1],
+                                           c.slot_ids[b:b + 1], c.block_table))
+    ref = torch.cat(parts, dim=1)
+    zero = torch.tensor([L == 0 for L in lens], device=cuda_device)
+    for splits in (0, 1, 5):
+        o = cabi.decode_attention(c.q, c.k, c.v, c.lens, c.slot_ids, c.block_table,
+                                  num_splits=splits)
+        assert _maxabs(o, ref) <= TOL
+        assert bool((o[0, zero] == 0).all())
 
 
 @pytest.mark.parametrize("splits", [4, 8, 16, 32, 64])

@@ -117,6 +117,18 @@ def test_config3_full(cuda_device):
         assert _maxabs(o, ref) <= TOL
 
 
+@pytest.mark.parametrize("seed", [1, 2, 3, 4])
+def test_config3_other_draws(seed, cuda_device):
+    # further draws of the config-3 distribution (32 sequences, half of them
+    # decode rows, chunks up to 512 tokens within a 2048-token budget, cached
+    # lengths up to 8192), at the default plan
+    chunk, kv = W.config3_shape(seed=seed)
+    c = W.make_mixed_case(chunk, kv, seed=seed, device=cuda_device, max_seqlen=2048,
+                          generate_on_device=True)
+    o = _run(c)
+    assert _maxabs(o, torch_mixed_fp32(c)) <= TOL
+
+
 def test_512_token_chunks(cuda_device):
     g = torch.Generator().manual_seed(1)
     kv = torch.randint(0, 8193, (4,), generator=g).tolist()
