@@ -70,7 +70,14 @@ constexpr int kStages = 5;
 constexpr int kMinBlocksPerSplit = 2;
 constexpr int kMaxSplits = 16;      // num_splits >= 1: key ranges per tile pair at most
 constexpr int kMaxPieces = 16;      // automatic plan: key ranges per tile pair at most
-constexpr int kWaves = 1;           // automatic plan: pieces of about 1/SMs of the work
+// Automatic plan: pieces of at most 1 / slots of the work, slots = 3/2 x SMs
+// (1, 5/4 and 2 x SMs measured: level, level and 8 % slower on 512-token
+// chunks; 3/2 is 2 % faster there and level on config 3).
+constexpr int kSlotsNum = 3;
+constexpr int kSlotsDen = 2;
+__host__ __device__ constexpr long long plan_slots(long long n_sm) {
+  return (n_sm * kSlotsNum + kSlotsDen - 1) / kSlotsDen;
+}
 constexpr int kPlanThreads = 1024;  // the planning kernel is one CTA
 constexpr int kPlanMaxBatch = 2048;
 constexpr int kSizeBuckets = kPlanThreads;  // pieces ordered by key blocks, largest first
@@ -347,7 +354,7 @@ __device__ __forceinline__ int plan_excl_scan(int v, int* s_warp, int& total) {
 // The work plan (one CTA). Units are (sequence, tile pair, kv head); a unit of
 // nb key blocks becomes k pieces of balanced key ranges: with num_splits >= 1
 // k = ceil(nb / max(ceil(nb / num_splits), 2)); automatically, ranges of at
-// most C = max(2, ceil(total blocks / (SMs * kWaves))) blocks, k <= kMaxPieces.
+// most C = max(2, ceil(total blocks / plan_slots(SMs))) blocks, k <= kMaxPieces.
 // Pieces are written largest first (a counting sort on their block count), so
 // the longest CTAs start first and the short ones fill the tail. Sequences
 // whose rows, slot or length are out of bounds raise a device error here and
@@ -426,7 +433,7 @@ __global__ void __launch_bounds__(kPlanThreads)
   if ((tid & 31) == 0 && mine != 0) atomicAdd(&s_blocks, mine);
   __syncthreads();
   const long long total_blocks = static_cast<long long>(s_blocks);
-  const long long slots = static_cast<long long>(p.n_sm) * kWaves;
+  const long long slots = plan_slots(p.n_sm);
   const long long C = max(static_cast<long long>(kMinBlocksPerSplit), (total_blocks + slots - 1) / slots);
   auto pieces_of = [&](int nb) {
     if (p.num_splits <= 0) return static_cast<int>(min(static_cast<long long>(kMaxPieces), (nb + C - 1) / C));
@@ -938,8 +945,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // lengths: a sequence has at most ceil(L / 36) <= L / 36 + 1 tile pairs; with
 // num_splits = S every pair is cut into at most S pieces; automatically a
 // pair of nb blocks gets at most nb / C + 1 pieces and only pairs longer than
-// C (fewer than total / C <= SMs * kWaves of them) are cut, so the pieces of
-// cut pairs number at most 2 * SMs * kWaves.
+// C (fewer than total / C <= plan_slots(SMs) of them) are cut, so the pieces of
+// cut pairs number at most 2 * plan_slots(SMs).
 struct PlanSizes {
   int64_t items, split, rec;
   size_t off_items, off_counters, off_records, bytes;
@@ -957,7 +964,7 @@ inline PlanSizes plan_sizes(int batch, int64_t total_tokens, int num_kv_heads, i
     ps.split = num_splits > 1 ? units : 0;
     ps.rec = num_splits > 1 ? num_splits * units : 0;
   } else {
-    const int64_t slots = static_cast<int64_t>(n_sm) * kWaves;
+    const int64_t slots = plan_slots(n_sm);
     ps.items = units + slots;
     ps.split = slots;
     ps.rec = 2 * slots;

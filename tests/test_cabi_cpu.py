@@ -101,13 +101,14 @@ def test_mixed_and_update_argument_checks():
         if splits >= 1:
             items, split, rec = splits * units, (units if splits > 1 else 0), \
                 (splits * units if splits > 1 else 0)
-        else:
-            items, split, rec = units + sms, sms, 2 * sms
+        else:  # automatic plan: 3/2 x SMs slots
+            slots = (sms * 3 + 1) // 2
+            items, split, rec = units + slots, slots, 2 * slots
         return 256 + r256(items * 32) + r256(split * 4) + rec * 256 * 66 * 4
     for args in ((4, 2048, 2, 1), (4, 2048, 2, 3), (4, 2048, 2, 0), (32, 2048, 2, 0),
                  (1, 1, 2, 16)):
         assert lib.cie_mixed_workspace_bytes(*args, -1) == plan_bytes(*args)
-    assert lib.cie_mixed_workspace_bytes(4, 2048, 2, 0, -1) < 24 << 20
+    assert lib.cie_mixed_workspace_bytes(4, 2048, 2, 0, -1) < 32 << 20
     assert lib.cie_kv_mixed_update(None, p, p, p, p, p, 4, 2, 64, 16, 10, 2048, 1024, 1152, 64,
                                    1152, 64, None) == -1
     # fused RoPE + KV write: qkv row 1152, cos/sin row 64, pool strides 2048 / 1024
