@@ -138,7 +138,7 @@ int cie_decode_attention_noalloc(const void* q, const void* k, const void* v,
  * `device` (its SM count sizes the automatic plan; -1: 148 SMs). The
  * workspace holds the work plan (made on the device by the call itself), a
  * counter per split tile pair and the fp32 partials of split pairs; about
- * 20 MB on 148 SMs with num_splits <= 0, nothing needs to start at zero. */
+ * 30 MB on 148 SMs with num_splits <= 0, nothing needs to start at zero. */
 size_t cie_mixed_workspace_bytes(int batch, int64_t total_tokens, int num_kv_heads,
                                  int num_splits, int device);
 
