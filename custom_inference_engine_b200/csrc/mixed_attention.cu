@@ -24,8 +24,9 @@
 //   warp 0       TMA producer: both Q tiles, then per key block the 8 K and
 //                8 V pages of this kv head (2 KiB boxes through the block
 //                table) into a 5-stage ring.
-//   warps 1, 2   MMA issuers of tile A and tile B (one thread each; warp 1
-//                also owns TMEM): S_x(j) = Q_x K_j^T as soon as K_j is in and
+//   warps 1, 2   MMA issuers of tile A and tile B (the whole warp runs the
+//                loop, one elected lane issues; warp 1 also owns TMEM):
+//                S_x(j) = Q_x K_j^T as soon as K_j is in and
 //                tile x's softmax has read S_x(j-1), then O_x += P_x(j-1)
 //                V_{j-1} once P_x(j-1) is published. S_x(j+1) is computed while
 //                the softmax of tile x still works on block j, and neither
