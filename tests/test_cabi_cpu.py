@@ -42,7 +42,10 @@ def test_host_only_queries():
     assert lib.cie_decode_workspace_bytes(8, 14, 64, 4) == 8 * 4 * 14 * 66 * 4
     assert lib.cie_decode_default_splits(0, -1) == 1
     assert lib.cie_decode_default_splits(256, -1) == 1
-    assert lib.cie_decode_default_splits(8, -1) == 37
+    assert lib.cie_decode_default_splits(8, -1) == 32    # 37 rounded down to a power of two
+    assert lib.cie_decode_default_splits(12, -1) == 24   # 24 is 3/2 of 16: kept
+    assert lib.cie_decode_default_splits(32, -1) == 8    # 9 -> 8
+    assert lib.cie_decode_default_splits(96, -1) == 3
     assert lib.cie_decode_default_splits(1, -1) == 64   # capped: the merge outgrows the gain
 
 
