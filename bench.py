@@ -27,7 +27,7 @@ Legs:
   cpu_baseline  the CPU oracle (torch fp32 gather + softmax) on the host's
             cores over a bounded sample of the same workload.
   mixed     mixed attention (512-token chunks, config 3): device time, e2e
-            through the C ABI, CPU oracle; timed first, before the decode loop.
+            through the C ABI, CPU oracle.
   sweep     config 2 (B x kv_len) and config 5 (split count) points, cold L2,
             beside the reference's own Triton kernels timed on the same GPU
             (``reference_triton``, baseline/time_reference_kernels.py).
@@ -413,8 +413,7 @@ def mixed_lines(dev, iters: int = 30, cpu: bool = True, e2e_steps: int = 50):
                "tensor_frac": tflops / peak, "peak_tflops": peak, "peak_source": src,
                "hbm_gbs": c.algorithmic_bytes() / (ms / 1e3) / 1e9,
                "chunks": c.chunk_lens(), "kv_lens": c.kv_lens.tolist(),
-               "l2": "flushed (256 MB read) before each call",
-               "order": "timed before the sustained decode loop"}
+               "l2": "flushed (256 MB read) before each call"}
 
         # e2e: the step's inputs from pinned host memory, o back to the host
         host = {n: getattr(c, n).cpu().pin_memory()
@@ -892,11 +891,6 @@ def run_ours(args, rank, world, local):
 
     dev = torch.device("cuda", torch.cuda.current_device())
     B, L = args.batch, args.kv_len
-    # The mixed lines are timed first, before the sustained decode loop has
-    # brought the GPU to its power cap (their calls last ~0.1 ms each).
-    mixed = None
-    if rank == 0 and not args.no_mixed:
-        mixed = mixed_lines(dev, cpu=world == 1 and not args.no_cpu_baseline)
     c = W.make_decode_case([L] * B, seed=100 + rank, device=dev, generate_on_device=True)
     S = args.splits if args.splits > 0 else cabi.decode_default_splits(B, dev.index)
     launches_per_step = 1 if S == 1 else 2
@@ -1027,7 +1021,9 @@ def run_ours(args, rank, world, local):
         if serving is not None:
             result["serving"] = serving
         if not args.no_mixed:
-            result["mixed"] = mixed
+            # after the serving legs: the CPU oracle it times leaves busy
+            # host threads behind, which slowed the host-bound prefill leg
+            result["mixed"] = mixed_lines(dev, cpu=world == 1 and not args.no_cpu_baseline)
         if world == 1 and not args.no_sweep:
             result["sweep"], ref = sweep_with_reference(dev, cpu=not args.no_cpu_baseline)
             result["reference_triton"] = ref
