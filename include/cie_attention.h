@@ -70,7 +70,8 @@ int cie_read_device_errors(int device, unsigned int* bits, int clear);
 
 /* Split count used when cie_decode_attention() is given num_splits <= 0:
  * enough (sequence, split) CTAs to keep every SM of `device` streaming
- * (two per SM), at most 64. */
+ * (two per SM), at most 64, rounded down to a power of two when it is less
+ * than 5/4 of one (148 SMs: batch 8 -> 32, 16 -> 16, 32 -> 8). */
 int cie_decode_default_splits(int batch, int device);
 
 /* Bytes of fp32 workspace the split path needs (0 when num_splits == 1). */
