@@ -84,19 +84,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Non-blocking: has the phase with the given parity completed?
-__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
 // Waits for the phase with the given parity to complete. Returns false (and
 // raises `err_bit`) when it has not completed within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int err_bit) {
@@ -216,28 +203,12 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16, issued by one thread.
-__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                           uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
-}
-
-// Warp-converged forms: every lane of the warp makes the call with the same
-// operands and the lane that elect.sync picks (the same lane every time) issues
-// the instruction, so a commit covers all MMAs issued through these forms by the
-// warp. A single-lane branch issuing the same MMAs is much slower when other
+// MMA issue and commit, warp-converged: every lane of the warp makes the call
+// with the same operands and the lane that elect.sync picks (the same lane every
+// time) issues the instruction, so a commit (an mbarrier arrival once all MMAs
+// the issuing thread started have completed) covers every MMA issued through
+// these calls by the warp. D[tmem] (+)= A * B, kind::f16, fp32 accumulation.
+// A single-lane branch issuing the same MMAs is much slower when other
 // warps keep the SM sub-partition's issue slots busy (B200, 24 MMAs + 6 commits of
 // the mixed-attention shapes with FMA-bound warps beside the issuer: 1.74 us from
 // one lane, 0.64 us converged; 0.73 / 0.57 us on an otherwise idle SM).
